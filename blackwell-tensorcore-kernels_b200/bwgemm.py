@@ -1,0 +1,244 @@
+"""Python face of libbwgemm.so (the C ABI declared in include/bwgemm.h).
+
+Used by bench.py, tests/ and __graft_entry__. Device memory and streams come from torch;
+every call goes through the C ABI with raw pointers, so what runs is the in-tree CUDA
+library. There is no fallback: if the shared library is missing or fails to load, every
+entry point raises.
+
+Reference interface mirrored (paths within waynehacking8/blackwell-tensorcore-kernels):
+  launch_<name>(A, B, C, M, N, K)  src/main.cu:18-39 -> launch(name, A, B, C) below, with the
+  same staging semantics (FP32 inputs are cast/quantised by the launcher, cached by pointer
+  identity and shape, src/gemm_mma.cu:152-168, src/gemm_mma_fp8.cu:230-264).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+import subprocess
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(_HERE)
+LIB_PATH = os.path.join(_HERE, "libbwgemm.so")
+HEADER = os.path.join(REPO, "include", "bwgemm.h")
+
+BW_OK, BW_ERR_INVALID, BW_ERR_CUDA, BW_ERR_TIMEOUT, BW_ERR_UNSUPPORTED = 0, 1, 2, 3, 4
+OUT_F32, OUT_BF16 = 0, 1
+SCALE_NONE, SCALE_FIXED8, SCALE_AMAX = 0, 1, 2
+FP4_PACKED, FP4_BYTE_SHL2 = 0, 1
+MX_UNIT_FIXED8, MX_BLOCK32 = 0, 1
+
+
+class BwError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"bwgemm error {code}: {msg}")
+        self.code = code
+
+
+_lib = None
+
+
+def build(tools: bool = False) -> None:
+    """Compile the library (and optionally gemm_bench / tc_rate_probe) for sm_100a in-tree."""
+    targets = ["all"] + (["tools"] if tools else [])
+    subprocess.run(["make", "-s", "-C", _HERE, *targets], check=True)
+
+
+def declared_functions() -> list[str]:
+    """Names of the entry points include/bwgemm.h declares."""
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return re.findall(r"^\s*(?:int|size_t|const char\*)\s+(bw_\w+)\s*\(", text, flags=re.M)
+
+
+def lib():
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(f"{LIB_PATH} is missing: run __graft_entry__.build() (make -C {_HERE})")
+    L = ctypes.CDLL(LIB_PATH)
+    P, I, LL = ctypes.c_void_p, ctypes.c_int, ctypes.c_longlong
+    sig = {
+        "bw_init": [I],
+        "bw_shutdown": [],
+        "bw_version": [],
+        "bw_num_sms": [I],
+        "bw_device_status": [P, P],
+        "bw_set_wait_budget_ns": [ctypes.c_ulonglong],
+        "bw_gemm_f16": [P, P, P, I, I, I, P],
+        "bw_gemm_f16_bt": [P, P, P, I, I, I, P],
+        "bw_gemm_fp8": [P, P, P, P, P, I, I, I, I, P],
+        "bw_gemm_mxfp4": [P, P, P, P, P, P, P, I, I, I, I, P],
+        "bw_gemm_fp4": [P, P, P, P, P, I, I, I, I, P],
+        "bw_quantize_f16": [P, P, LL, P],
+        "bw_quantize_fp8": [P, P, P, I, I, I, I, P],
+        "bw_quantize_fp4": [P, P, P, I, I, I, I, I, P],
+        "bw_quantize_mxfp4": [P, P, P, I, I, I, I, P],
+        "bw_unshard_columns": [P, P, I, I, I, P],
+    }
+    for name, args in sig.items():
+        f = getattr(L, name)
+        f.argtypes = args
+        f.restype = I
+    L.bw_last_error_string.argtypes = []
+    L.bw_last_error_string.restype = ctypes.c_char_p
+    L.bw_sf_bytes.argtypes = [I, I]
+    L.bw_sf_bytes.restype = ctypes.c_size_t
+    L.bw_sf_offset.argtypes = [I, I, I]
+    L.bw_sf_offset.restype = ctypes.c_size_t
+    _lib = L
+    return L
+
+
+def _check(rc: int) -> None:
+    if rc != BW_OK:
+        raise BwError(rc, lib().bw_last_error_string().decode(errors="replace"))
+
+
+def _ptr(t) -> int | None:
+    if t is None:
+        return None
+    return t.data_ptr()
+
+
+def _stream(stream) -> int | None:
+    import torch
+
+    if stream is None:
+        return torch.cuda.current_stream().cuda_stream
+    if isinstance(stream, int):
+        return stream
+    return stream.cuda_stream
+
+
+# ------------------------------------------------------------------ runtime
+def init(device: int = 0) -> None:
+    _check(lib().bw_init(device))
+
+
+def device_status(stream=None) -> int:
+    out = ctypes.c_int(0)
+    rc = lib().bw_device_status(_stream(stream), ctypes.byref(out))
+    if rc not in (BW_OK, BW_ERR_TIMEOUT):
+        _check(rc)
+    return out.value
+
+
+def set_wait_budget_ns(ns: int) -> None:
+    _check(lib().bw_set_wait_budget_ns(int(ns)))
+
+
+def sf_bytes(outer: int, K: int) -> int:
+    return int(lib().bw_sf_bytes(outer, K))
+
+
+# ------------------------------------------------------------------ GEMMs
+def gemm_f16(A, B, C=None, stream=None, b_transposed: bool = False):
+    """C (fp32) = A (fp16 MxK) x B (fp16 KxN, or NxK when b_transposed)."""
+    import torch
+
+    M, K = A.shape
+    N = B.shape[0] if b_transposed else B.shape[1]
+    if C is None:
+        C = torch.empty((M, N), dtype=torch.float32, device=A.device)
+    fn = lib().bw_gemm_f16_bt if b_transposed else lib().bw_gemm_f16
+    _check(fn(_ptr(A), _ptr(B), _ptr(C), M, N, K, _stream(stream)))
+    return C
+
+
+def gemm_fp8(A, Bt, scale_a=None, scale_b=None, C=None, out_dtype=OUT_BF16, stream=None):
+    """C = (A (e4m3 MxK) x Bt^T (e4m3 NxK)) * scale_a * scale_b."""
+    import torch
+
+    M, K = A.shape
+    N = Bt.shape[0]
+    if C is None:
+        C = torch.empty((M, N), dtype=torch.bfloat16 if out_dtype == OUT_BF16 else torch.float32, device=A.device)
+    _check(lib().bw_gemm_fp8(_ptr(A), _ptr(Bt), _ptr(scale_a), _ptr(scale_b), _ptr(C), out_dtype, M, N, K,
+                             _stream(stream)))
+    return C
+
+
+def gemm_mxfp4(A, Bt, sfa, sfb, K: int, scale_a=None, scale_b=None, C=None, out_dtype=OUT_BF16, stream=None):
+    import torch
+
+    M, N = A.shape[0], Bt.shape[0]
+    if C is None:
+        C = torch.empty((M, N), dtype=torch.bfloat16 if out_dtype == OUT_BF16 else torch.float32, device=A.device)
+    _check(lib().bw_gemm_mxfp4(_ptr(A), _ptr(Bt), _ptr(sfa), _ptr(sfb), _ptr(scale_a), _ptr(scale_b), _ptr(C),
+                               out_dtype, M, N, K, _stream(stream)))
+    return C
+
+
+def gemm_fp4(A, Bt, K: int, scale_a=None, scale_b=None, C=None, out_dtype=OUT_BF16, stream=None):
+    import torch
+
+    M, N = A.shape[0], Bt.shape[0]
+    if C is None:
+        C = torch.empty((M, N), dtype=torch.bfloat16 if out_dtype == OUT_BF16 else torch.float32, device=A.device)
+    _check(lib().bw_gemm_fp4(_ptr(A), _ptr(Bt), _ptr(scale_a), _ptr(scale_b), _ptr(C), out_dtype, M, N, K,
+                             _stream(stream)))
+    return C
+
+
+# ------------------------------------------------------------------ quantisers
+def quantize_f16(src, dst=None, stream=None):
+    import torch
+
+    if dst is None:
+        dst = torch.empty(src.shape, dtype=torch.float16, device=src.device)
+    _check(lib().bw_quantize_f16(_ptr(src), _ptr(dst), src.numel(), _stream(stream)))
+    return dst
+
+
+def quantize_fp8(src, transpose=False, scale_mode=SCALE_AMAX, dst=None, scale_out=None, stream=None):
+    import torch
+
+    rows, cols = src.shape
+    if dst is None:
+        dst = torch.empty((cols, rows) if transpose else (rows, cols), dtype=torch.uint8, device=src.device)
+    if scale_out is None:
+        scale_out = torch.empty(1, dtype=torch.float32, device=src.device)
+    _check(lib().bw_quantize_fp8(_ptr(src), _ptr(dst), _ptr(scale_out), rows, cols, int(transpose), scale_mode,
+                                 _stream(stream)))
+    return dst, scale_out
+
+
+def quantize_fp4(src, transpose=False, scale_mode=SCALE_AMAX, container=FP4_PACKED, dst=None, scale_out=None,
+                 stream=None):
+    import torch
+
+    rows, cols = src.shape
+    orows, ocols = (cols, rows) if transpose else (rows, cols)
+    if dst is None:
+        dst = torch.empty((orows, ocols if container == FP4_BYTE_SHL2 else ocols // 2), dtype=torch.uint8,
+                          device=src.device)
+    if scale_out is None:
+        scale_out = torch.empty(1, dtype=torch.float32, device=src.device)
+    _check(lib().bw_quantize_fp4(_ptr(src), _ptr(dst), _ptr(scale_out), rows, cols, int(transpose), scale_mode,
+                                 container, _stream(stream)))
+    return dst, scale_out
+
+
+def quantize_mxfp4(src, transpose=False, mode=MX_BLOCK32, dst=None, sf=None, stream=None):
+    import torch
+
+    rows, cols = src.shape
+    K, outer = (rows, cols) if transpose else (cols, rows)
+    if dst is None:
+        dst = torch.empty((outer, K // 2), dtype=torch.uint8, device=src.device)
+    if sf is None:
+        sf = torch.empty(sf_bytes(outer, K), dtype=torch.uint8, device=src.device)
+    _check(lib().bw_quantize_mxfp4(_ptr(src), _ptr(dst), _ptr(sf), rows, cols, int(transpose), mode,
+                                   _stream(stream)))
+    return dst, sf
+
+
+def unshard_columns(C_shardmajor, M: int, N: int, world: int, out=None, stream=None):
+    import torch
+
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float32, device=C_shardmajor.device)
+    _check(lib().bw_unshard_columns(_ptr(C_shardmajor), _ptr(out), M, N, world, _stream(stream)))
+    return out

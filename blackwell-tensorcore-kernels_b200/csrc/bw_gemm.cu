@@ -1,0 +1,195 @@
+// GEMM entry points of the C ABI: argument checks, TMA descriptors, tile-shape choice and
+// launch of the persistent tcgen05 kernel (bw_gemm_kernel.cuh).
+#include <cstdlib>
+
+#include "bw_gemm_kernel.cuh"
+#include "bw_runtime.cuh"
+
+namespace bw {
+namespace {
+
+int env_int(const char* name, int dflt) {
+  const char* s = getenv(name);
+  if (!s || !*s) return dflt;
+  return atoi(s);
+}
+
+template <Kind KIND, bool B_MN, int BN, int STAGES, int ACC_BUFS, Out OUT>
+int launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p, cudaStream_t stream, const DeviceState& d) {
+  using Cfg = GemmCfg<KIND, B_MN, BN, STAGES, ACC_BUFS>;
+  auto kern = bw_tc_gemm_kernel<KIND, B_MN, BN, STAGES, ACC_BUFS, OUT>;
+  static bool attr_done[64] = {};
+  int dev = 0;
+  BW_CUDA(cudaGetDevice(&dev));
+  if (!attr_done[dev & 63]) {
+    BW_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
+    attr_done[dev & 63] = true;
+  }
+  const int tiles = ((p.M + kBM - 1) / kBM) * ((p.N + BN - 1) / BN);
+  int grid = tiles < d.sms ? tiles : d.sms;
+  const int cap = env_int("BW_MAX_CTAS", 0);
+  if (cap > 0 && grid > cap) grid = cap;
+  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, p);
+  BW_CUDA(cudaGetLastError());
+  return BW_OK;
+}
+
+GemmParams base_params(const DeviceState& d, void* C, int M, int N, int K) {
+  GemmParams p{};
+  p.C = C;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.ldc = N;
+  p.group_m = env_int("BW_GROUP_M", 16);
+  if (p.group_m < 1) p.group_m = 1;
+  p.status = d.status;
+  p.budget_ns = wait_budget_ns();
+  return p;
+}
+
+int check_common(const void* A, const void* B, const void* C, int M, int N, int K) {
+  if (M < 0 || N < 0 || K < 0) return set_error(BW_ERR_INVALID, "negative size M=%d N=%d K=%d", M, N, K);
+  if (M == 0 || N == 0) return BW_OK;
+  if (!C) return set_error(BW_ERR_INVALID, "C is null");
+  if (K > 0 && (!A || !B)) return set_error(BW_ERR_INVALID, "A or B is null");
+  if (!aligned16(A) || !aligned16(B) || !aligned16(C))
+    return set_error(BW_ERR_INVALID, "A, B and C must be 16-byte aligned");
+  return BW_OK;
+}
+
+// Prefer 128 x 256 tiles; fall back to 128 x 128 when the wide tiles would leave SMs idle.
+bool use_narrow(int M, int N, const DeviceState& d) {
+  const int forced = env_int("BW_TILE_N", 0);
+  if (forced == 128) return true;
+  if (forced == 256) return false;
+  const long tiles256 = static_cast<long>((M + 127) / 128) * ((N + 255) / 256);
+  return tiles256 < d.sms;
+}
+
+int gemm_f16_impl(const void* A, const void* B, float* C, int M, int N, int K, cudaStream_t s, bool b_mn) {
+  int r = check_common(A, B, C, M, N, K);
+  if (r != BW_OK || M == 0 || N == 0) return r;
+  if (K % 8 != 0 || N % 8 != 0)
+    return set_error(BW_ERR_INVALID, "fp16 GEMM needs K %% 8 == 0 and N %% 8 == 0 (got N=%d K=%d)", N, K);
+  DeviceState* d;
+  if ((r = ensure_device(&d)) != BW_OK) return r;
+  if (K == 0) { BW_CUDA(cudaMemsetAsync(C, 0, sizeof(float) * size_t(M) * N, s)); return BW_OK; }
+  const bool narrow = use_narrow(M, N, *d);
+  const int bn = narrow ? 128 : 256;
+  CUtensorMap ta, tb;
+  if ((r = make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, A, K, M, uint64_t(K) * 2, 64, 128)) != BW_OK) return r;
+  if (b_mn) r = make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, B, N, K, uint64_t(N) * 2, 64, 64);
+  else r = make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, B, K, N, uint64_t(K) * 2, 64, bn);
+  if (r != BW_OK) return r;
+  GemmParams p = base_params(*d, C, M, N, K);
+  if (b_mn) {
+    if (narrow) return launch<Kind::F16, true, 128, 6, 2, Out::F32>(ta, tb, p, s, *d);
+    return launch<Kind::F16, true, 256, 4, 2, Out::F32>(ta, tb, p, s, *d);
+  }
+  if (narrow) return launch<Kind::F16, false, 128, 6, 2, Out::F32>(ta, tb, p, s, *d);
+  return launch<Kind::F16, false, 256, 4, 2, Out::F32>(ta, tb, p, s, *d);
+}
+
+size_t out_elem_bytes(int out_dtype) { return out_dtype == BW_OUT_BF16 ? 2 : 4; }
+
+int gemm_fp8_impl(const uint8_t* A, const uint8_t* Bt, const float* sa, const float* sb, void* C, int out_dtype,
+                  int M, int N, int K, cudaStream_t s) {
+  int r = check_common(A, Bt, C, M, N, K);
+  if (r != BW_OK || M == 0 || N == 0) return r;
+  if (out_dtype != BW_OUT_F32 && out_dtype != BW_OUT_BF16) return set_error(BW_ERR_INVALID, "bad out_dtype %d", out_dtype);
+  if (K % 16 != 0) return set_error(BW_ERR_INVALID, "fp8 GEMM needs K %% 16 == 0 (got %d)", K);
+  if (N % 8 != 0) return set_error(BW_ERR_INVALID, "fp8 GEMM needs N %% 8 == 0 (got %d)", N);
+  DeviceState* d;
+  if ((r = ensure_device(&d)) != BW_OK) return r;
+  if (K == 0) { BW_CUDA(cudaMemsetAsync(C, 0, out_elem_bytes(out_dtype) * size_t(M) * N, s)); return BW_OK; }
+  const bool narrow = use_narrow(M, N, *d);
+  const int bn = narrow ? 128 : 256;
+  CUtensorMap ta, tb;
+  if ((r = make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, A, K, M, uint64_t(K), 128, 128)) != BW_OK) return r;
+  if ((r = make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, Bt, K, N, uint64_t(K), 128, bn)) != BW_OK) return r;
+  GemmParams p = base_params(*d, C, M, N, K);
+  p.scale_a = sa;
+  p.scale_b = sb;
+  if (out_dtype == BW_OUT_F32) {
+    if (narrow) return launch<Kind::F8, false, 128, 6, 2, Out::F32>(ta, tb, p, s, *d);
+    return launch<Kind::F8, false, 256, 4, 2, Out::F32>(ta, tb, p, s, *d);
+  }
+  if (narrow) return launch<Kind::F8, false, 128, 6, 2, Out::BF16>(ta, tb, p, s, *d);
+  return launch<Kind::F8, false, 256, 4, 2, Out::BF16>(ta, tb, p, s, *d);
+}
+
+int gemm_mxf4_impl(const uint8_t* A, const uint8_t* Bt, const uint8_t* sfa, const uint8_t* sfb, const float* sa,
+                   const float* sb, void* C, int out_dtype, int M, int N, int K, cudaStream_t s, bool unit_sf) {
+  int r = check_common(A, Bt, C, M, N, K);
+  if (r != BW_OK || M == 0 || N == 0) return r;
+  if (out_dtype != BW_OUT_F32 && out_dtype != BW_OUT_BF16) return set_error(BW_ERR_INVALID, "bad out_dtype %d", out_dtype);
+  if (K % 32 != 0) return set_error(BW_ERR_INVALID, "fp4 GEMM needs K %% 32 == 0 (got %d)", K);
+  if (N % 8 != 0) return set_error(BW_ERR_INVALID, "fp4 GEMM needs N %% 8 == 0 (got %d)", N);
+  if (unit_sf) { sfa = nullptr; sfb = nullptr; }
+  else if (K > 0 && (!sfa || !sfb)) return set_error(BW_ERR_INVALID, "scale-factor pointers are null");
+  if (!unit_sf && K > 0 && (!aligned16(sfa) || !aligned16(sfb))) return set_error(BW_ERR_INVALID, "scale factors must be 16-byte aligned");
+  DeviceState* d;
+  if ((r = ensure_device(&d)) != BW_OK) return r;
+  if (K == 0) { BW_CUDA(cudaMemsetAsync(C, 0, out_elem_bytes(out_dtype) * size_t(M) * N, s)); return BW_OK; }
+  CUtensorMap ta, tb;
+  if ((r = make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, A, K / 2, M, uint64_t(K / 2), 128, 128)) != BW_OK) return r;
+  if ((r = make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, Bt, K / 2, N, uint64_t(K / 2), 128, 128)) != BW_OK) return r;
+  GemmParams p = base_params(*d, C, M, N, K);
+  p.scale_a = sa;
+  p.scale_b = sb;
+  p.sfa = sfa;
+  p.sfb = sfb;
+  p.sf_kgroups = ((K + 31) / 32 + 3) / 4;
+  if (out_dtype == BW_OUT_F32) return launch<Kind::MXF4, false, 128, 6, 2, Out::F32>(ta, tb, p, s, *d);
+  return launch<Kind::MXF4, false, 128, 6, 2, Out::BF16>(ta, tb, p, s, *d);
+}
+
+}  // namespace
+}  // namespace bw
+
+using namespace bw;
+
+extern "C" {
+
+int bw_gemm_f16(const void* A, const void* B, float* C, int M, int N, int K, void* stream) {
+  return gemm_f16_impl(A, B, C, M, N, K, static_cast<cudaStream_t>(stream), true);
+}
+
+int bw_gemm_f16_bt(const void* A, const void* Bt, float* C, int M, int N, int K, void* stream) {
+  return gemm_f16_impl(A, Bt, C, M, N, K, static_cast<cudaStream_t>(stream), false);
+}
+
+int bw_gemm_fp8(const uint8_t* A, const uint8_t* Bt, const float* scale_a, const float* scale_b, void* C,
+                int out_dtype, int M, int N, int K, void* stream) {
+  return gemm_fp8_impl(A, Bt, scale_a, scale_b, C, out_dtype, M, N, K, static_cast<cudaStream_t>(stream));
+}
+
+int bw_gemm_mxfp4(const uint8_t* A, const uint8_t* Bt, const uint8_t* sfA, const uint8_t* sfB,
+                  const float* scale_a, const float* scale_b, void* C, int out_dtype, int M, int N, int K,
+                  void* stream) {
+  return gemm_mxf4_impl(A, Bt, sfA, sfB, scale_a, scale_b, C, out_dtype, M, N, K, static_cast<cudaStream_t>(stream),
+                        false);
+}
+
+int bw_gemm_fp4(const uint8_t* A, const uint8_t* Bt, const float* scale_a, const float* scale_b, void* C,
+                int out_dtype, int M, int N, int K, void* stream) {
+  return gemm_mxf4_impl(A, Bt, nullptr, nullptr, scale_a, scale_b, C, out_dtype, M, N, K,
+                        static_cast<cudaStream_t>(stream), true);
+}
+
+size_t bw_sf_bytes(int outer, int K) {
+  if (outer <= 0 || K <= 0) return 0;
+  const size_t rb = (static_cast<size_t>(outer) + 127) / 128;
+  const size_t kg = ((static_cast<size_t>(K) + 31) / 32 + 3) / 4;
+  return rb * kg * 512;
+}
+
+size_t bw_sf_offset(int row, int kblock, int K) {
+  const size_t kg = ((static_cast<size_t>(K) + 31) / 32 + 3) / 4;
+  const size_t atom = (static_cast<size_t>(row) / 128) * kg + static_cast<size_t>(kblock) / 4;
+  const int r = row % 128;
+  return atom * 512 + (r % 32) * 16 + (r / 32) * 4 + (kblock % 4);
+}
+
+}  // extern "C"

@@ -1,0 +1,341 @@
+// Persistent, warp-specialised tcgen05 GEMM for sm_100a.
+//
+// Replaces the reference's hot kernels:
+//   gemm_mma_t      (src/gemm_mma.cu:23-141)      FP16 in / FP32 acc, A MxK, B KxN row-major
+//   gemm_wmma_t     (src/gemm_wmma.cu:29-104)     same math through WMMA
+//   gemm_lowprec_t  (src/gemm_mma_fp8.cu:89-223)  E4M3 / E2M1 / packed E2M1, "TN" layout
+//
+// One CTA per SM runs for the whole problem and walks output tiles of 128 x BN.
+//   warp 0      TMA producer: one elected lane streams A/B k-slabs (128 B wide, 128B-swizzled)
+//               into a STAGES-deep shared-memory ring guarded by full/empty mbarriers.
+//   warp 1      allocates Tensor Memory; one elected lane issues tcgen05.mma for every
+//               k-slab (4 MMAs of 32 bytes of K each) into one of ACC_BUFS TMEM accumulators
+//               and commits slab release / accumulator-ready through tcgen05.commit.
+//   warps 2..5  epilogue: tcgen05.ld the 128 x BN FP32 accumulator (one row per thread),
+//               release the TMEM buffer, scale, convert and store C.
+// With ACC_BUFS = 2 the epilogue of tile i overlaps the main loop of tile i+1.
+//
+// Operand formats (KIND):
+//   F16   A: MxK fp16 (K-major). B: KxN fp16 (N-major, B_MN = true) or NxK (B_MN = false).
+//   F8    A: MxK e4m3, Bt: NxK e4m3 (both K-major).
+//   MXF4  A: MxK/2 packed e2m1, Bt: NxK/2 packed e2m1, plus UE8M0 scale factors, one per
+//         32 K elements, in the 128x4 tiled layout (see bw_sf_offset in bwgemm.h).
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "bw_ptx.cuh"
+
+namespace bw {
+
+enum class Kind : int { F16 = 0, F8 = 1, MXF4 = 2 };
+enum class Out : int { F32 = 0, BF16 = 1 };
+
+constexpr int kBM = 128;          // rows of A per tile (one TMEM lane per row)
+constexpr int kSlabBytes = 128;   // bytes of K per k-slab row (one 128B swizzle atom)
+constexpr int kThreads = 192;     // 6 warps
+constexpr int kEpiWarps = 4;
+
+template <Kind KIND>
+struct KindTraits;
+template <>
+struct KindTraits<Kind::F16> {
+  static constexpr int kElemsPerSlab = 64;  // 64 fp16 = 128 B
+  static constexpr uint32_t kFmt = 0;       // F16
+};
+template <>
+struct KindTraits<Kind::F8> {
+  static constexpr int kElemsPerSlab = 128;  // 128 e4m3
+  static constexpr uint32_t kFmt = 0;        // E4M3
+};
+template <>
+struct KindTraits<Kind::MXF4> {
+  static constexpr int kElemsPerSlab = 256;  // 256 packed e2m1 = 128 B
+  static constexpr uint32_t kFmt = 1;
+};
+
+struct GemmParams {
+  void* C;
+  int M, N, K;
+  int ldc;                     // elements between C rows
+  const float* scale_a;        // optional per-tensor scales (device, may be null)
+  const float* scale_b;
+  const uint8_t* sfa;          // MXF4: A scale factors, tiled 128x4 layout
+  const uint8_t* sfb;          // MXF4: B scale factors
+  int sf_kgroups;              // MXF4: number of 4-block K groups per 128-row block
+  int group_m;                 // raster: tile rows per group
+  int* status;                 // device status word
+  unsigned long long budget_ns;
+};
+
+template <Kind KIND, bool B_MN, int BN, int STAGES, int ACC_BUFS>
+struct GemmCfg {
+  static constexpr int kABytes = kBM * kSlabBytes;               // 16 KB
+  static constexpr int kBBytes = BN * kSlabBytes;                // BN x 128 B
+  static constexpr int kSfaBytes = (KIND == Kind::MXF4) ? 1024 : 0;        // 2 atoms of 512 B
+  static constexpr int kSfbBytes = (KIND == Kind::MXF4) ? (BN / 128) * 1024 : 0;
+  static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;
+  static constexpr int kAccCols = ACC_BUFS * BN;
+  static constexpr int kSfaCols = (KIND == Kind::MXF4) ? 8 : 0;
+  static constexpr int kSfbCols = (KIND == Kind::MXF4) ? 8 * (BN / 128) : 0;
+  static constexpr int kNeedCols = kAccCols + kSfaCols + kSfbCols;
+  static constexpr int kTmemCols = kNeedCols <= 32 ? 32 : kNeedCols <= 64 ? 64 : kNeedCols <= 128 ? 128
+                                   : kNeedCols <= 256 ? 256 : 512;
+  static_assert(kNeedCols <= 512, "TMEM budget exceeded");
+  static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN");
+  static_assert(KIND != Kind::MXF4 || BN % 128 == 0, "MXF4 tiles cover whole 128-row SF blocks");
+  static constexpr int kBarOffset = STAGES * kStageBytes;
+  // full[S], empty[S], accfull[ACC], accempty[ACC], teardown
+  static constexpr int kNumBars = 2 * STAGES + 2 * ACC_BUFS + 1;
+  static constexpr int kSmemBytes = kBarOffset + kNumBars * 8 + 16 + 1024;  // + align slack
+};
+
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int group_m, int& tm, int& tn) {
+  const int per_group = group_m * tiles_n;
+  const int g = t / per_group;
+  const int first_m = g * group_m;
+  const int gm = min(tiles_m - first_m, group_m);
+  const int r = t - g * per_group;
+  tm = first_m + r % gm;
+  tn = r / gm;
+}
+
+template <Kind KIND, bool B_MN, int BN, int STAGES, int ACC_BUFS, Out OUT>
+__global__ void __launch_bounds__(kThreads, 1)
+    bw_tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      const GemmParams p) {
+  using Cfg = GemmCfg<KIND, B_MN, BN, STAGES, ACC_BUFS>;
+  constexpr int KE = KindTraits<KIND>::kElemsPerSlab;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kBarOffset);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* accfull = bars + 2 * STAGES;
+  uint64_t* accempty = bars + 2 * STAGES + ACC_BUFS;
+  uint64_t* teardown = bars + 2 * STAGES + 2 * ACC_BUFS;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::kNumBars);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int tiles_m = (p.M + kBM - 1) / kBM;
+  const int tiles_n = (p.N + BN - 1) / BN;
+  const int num_tiles = tiles_m * tiles_n;
+  const int nk = (p.K + KE - 1) / KE;
+  const WaitCtl wc{abort_flag, p.status, p.budget_ns};
+
+  if constexpr (KIND == Kind::MXF4) {
+    // Scale-factor slots a tail slab does not refill must hold finite scales (they
+    // multiply zero-filled operands); start them at 0x7f = 2^0.
+    for (int s = 0; s < STAGES; ++s) {
+      uint32_t* sf = reinterpret_cast<uint32_t*>(smem + s * Cfg::kStageBytes + Cfg::kABytes + Cfg::kBBytes);
+      for (int i = threadIdx.x; i < (Cfg::kSfaBytes + Cfg::kSfbBytes) / 4; i += kThreads) sf[i] = 0x7f7f7f7fu;
+    }
+    fence_proxy_async_smem();
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    for (int b = 0; b < ACC_BUFS; ++b) { mbar_init(&accfull[b], 1); mbar_init(&accempty[b], kEpiWarps * 32); }
+    mbar_init(teardown, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) { tma_prefetch_desc(&tmA); tma_prefetch_desc(&tmB); }
+  if (warp == 1) { tmem_alloc(tmem_slot, Cfg::kTmemCols); tmem_relinquish(); }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      const uint64_t pol_a = l2_policy_evict_last();
+      const uint64_t pol_b = l2_policy_evict_last();
+      int s = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        int tm, tn;
+        tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&empty[s], ph ^ 1, wc, 1)) { ok = false; break; }
+          uint8_t* sA = smem + s * Cfg::kStageBytes;
+          uint8_t* sB = sA + Cfg::kABytes;
+          uint32_t tx = Cfg::kABytes + Cfg::kBBytes;
+          uint32_t sfa_bytes = 0, sfb_rbs = 0;
+          if (KIND == Kind::MXF4 && p.sfa != nullptr) {
+            // A k-slab of 256 K covers SF groups 2kb, 2kb+1; the last slab may have only one,
+            // and the last B tile may cover fewer than BN/128 row blocks.
+            sfa_bytes = (2 * kb + 1 < p.sf_kgroups) ? 1024u : 512u;
+            const int rb_total = (p.N + 127) / 128;
+            sfb_rbs = min(BN / 128, rb_total - tn * (BN / 128));
+            tx += sfa_bytes * (1 + sfb_rbs);
+          }
+          mbar_arrive_expect_tx(&full[s], tx);
+          tma_load_2d(&tmA, &full[s], sA, kb * KE, tm * kBM, pol_a);
+          if constexpr (B_MN) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(&tmB, &full[s], sB + j * 64 * kSlabBytes, tn * BN + 64 * j, kb * 64, pol_b);
+          } else {
+            tma_load_2d(&tmB, &full[s], sB, kb * KE, tn * BN, pol_b);
+          }
+          if (KIND == Kind::MXF4 && p.sfa != nullptr) {
+            // Scale factors: tiled layout = [row block][k group of 4 SF][512 B]. One stage
+            // covers 256 K = 8 SF per row = 2 k groups = 1 KB contiguous per row block.
+            uint8_t* sSfa = sB + Cfg::kBBytes;
+            uint8_t* sSfb = sSfa + Cfg::kSfaBytes;
+            const size_t kg0 = static_cast<size_t>(kb) * 2;
+            bulk_load(sSfa, p.sfa + (static_cast<size_t>(tm) * p.sf_kgroups + kg0) * 512, sfa_bytes, &full[s]);
+            for (uint32_t rb = 0; rb < sfb_rbs; ++rb)
+              bulk_load(sSfb + rb * 1024,
+                        p.sfb + (static_cast<size_t>(tn * (BN / 128) + rb) * p.sf_kgroups + kg0) * 512, sfa_bytes,
+                        &full[s]);
+          }
+          if (++s == STAGES) { s = 0; ph ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      uint32_t idesc;
+      if constexpr (KIND == Kind::MXF4) idesc = 0;  // built per k-step (scale-factor byte ids)
+      else idesc = idesc_dense(KindTraits<KIND>::kFmt, KindTraits<KIND>::kFmt, B_MN, kBM, BN);
+      const uint32_t tmem_sfa = tmem_base + Cfg::kAccCols;
+      const uint32_t tmem_sfb = tmem_sfa + Cfg::kSfaCols;
+      int s = 0;
+      uint32_t ph = 0;
+      int local = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++local) {
+        const int b = local % ACC_BUFS;
+        const uint32_t aph = (local / ACC_BUFS) & 1;
+        if (!mbar_wait(&accempty[b], aph ^ 1, wc, 2)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + b * BN;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&full[s], ph, wc, 3)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t aaddr = smem_u32(smem + s * Cfg::kStageBytes);
+          const uint32_t baddr = aaddr + Cfg::kABytes;
+          if (KIND == Kind::MXF4 && (p.sfa != nullptr || (kb == 0 && local == 0))) {
+            // Per-slab scale factors; with no SF arrays (plain FP4) the 0x7f-filled slots are
+            // copied once and every block scale stays 2^0.
+            const uint32_t sfa_s = baddr + Cfg::kBBytes;
+            const uint32_t sfb_s = sfa_s + Cfg::kSfaBytes;
+            // 512 B atom = 32 rows x 16 B, no swizzle; replicated to the 4 lane quarters.
+#pragma unroll
+            for (int a = 0; a < 2; ++a) {
+              tmem_cp_32x128b_warpx4(tmem_sfa + a * 4, sdesc_noswz(sfa_s + a * 512, 16, 128));
+#pragma unroll
+              for (int rb = 0; rb < BN / 128; ++rb)
+                tmem_cp_32x128b_warpx4(tmem_sfb + a * (BN / 128) * 4 + rb * 4,
+                                       sdesc_noswz(sfb_s + rb * 1024 + a * 512, 16, 128));
+            }
+          }
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
+            const uint64_t adesc = sdesc_sw128(aaddr + k * 32, 16, 1024);
+            uint64_t bdesc;
+            if constexpr (B_MN) bdesc = sdesc_sw128(baddr + k * 16 * kSlabBytes, 64 * kSlabBytes, 1024);
+            else bdesc = sdesc_sw128(baddr + k * 32, 16, 1024);
+            if constexpr (KIND == Kind::F16) {
+              umma_f16(d_tmem, adesc, bdesc, idesc, acc);
+            } else if constexpr (KIND == Kind::F8) {
+              umma_f8f6f4(d_tmem, adesc, bdesc, idesc, acc);
+            } else {
+              // k-step k uses SF blocks 2k, 2k+1 = atom k/2, bytes (2k)%4 .. +1.
+              const uint32_t sf_id = (2 * k) & 3;
+              const uint32_t id = idesc_mxf4(kBM, BN, sf_id, sf_id);
+              umma_mxf4(d_tmem, adesc, bdesc, id, tmem_sfa + (k >> 1) * 4,
+                        tmem_sfb + (k >> 1) * (BN / 128) * 4, acc);
+            }
+          }
+          umma_commit(&empty[s]);
+          if (++s == STAGES) { s = 0; ph ^= 1; }
+        }
+        if (ok) umma_commit(&accfull[b]);
+      }
+      // Make sure every MMA this thread issued has retired before TMEM is released.
+      umma_commit(teardown);
+      mbar_wait(teardown, 0, WaitCtl{abort_flag, p.status, p.budget_ns}, 4);
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int q = warp & 3;                  // TMEM lane quarter this warp may access
+    const int row_in_tile = q * 32 + lane;
+    float alpha = 1.f;
+    if (p.scale_a) alpha *= __ldg(p.scale_a);
+    if (p.scale_b) alpha *= __ldg(p.scale_b);
+    int local = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
+      int tm, tn;
+      tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
+      const int b = local % ACC_BUFS;
+      const uint32_t aph = (local / ACC_BUFS) & 1;
+      if (!mbar_wait(&accfull[b], aph, wc, 5)) break;
+      tc_fence_after();
+      const int row = tm * kBM + row_in_tile;
+      const int col0 = tn * BN;
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tbase + c * 32, r);
+        tmem_ld_wait();
+        if (c == BN / 32 - 1) { tc_fence_before(); mbar_arrive(&accempty[b]); }
+        const int col = col0 + c * 32;
+        if (row < p.M) {
+          if constexpr (OUT == Out::F32) {
+            float* dst = reinterpret_cast<float*>(p.C) + static_cast<size_t>(row) * p.ldc + col;
+            if (col + 32 <= p.N) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 4) {
+                float4 v = make_float4(__uint_as_float(r[j]) * alpha, __uint_as_float(r[j + 1]) * alpha,
+                                       __uint_as_float(r[j + 2]) * alpha, __uint_as_float(r[j + 3]) * alpha);
+                *reinterpret_cast<float4*>(dst + j) = v;
+              }
+            } else {
+              for (int j = 0; j < 32; ++j)
+                if (col + j < p.N) dst[j] = __uint_as_float(r[j]) * alpha;
+            }
+          } else {
+            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.C) + static_cast<size_t>(row) * p.ldc + col;
+            if (col + 32 <= p.N) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 8) {
+                uint4 v;
+                __nv_bfloat162 h0 = __floats2bfloat162_rn(__uint_as_float(r[j]) * alpha, __uint_as_float(r[j + 1]) * alpha);
+                __nv_bfloat162 h1 = __floats2bfloat162_rn(__uint_as_float(r[j + 2]) * alpha, __uint_as_float(r[j + 3]) * alpha);
+                __nv_bfloat162 h2 = __floats2bfloat162_rn(__uint_as_float(r[j + 4]) * alpha, __uint_as_float(r[j + 5]) * alpha);
+                __nv_bfloat162 h3 = __floats2bfloat162_rn(__uint_as_float(r[j + 6]) * alpha, __uint_as_float(r[j + 7]) * alpha);
+                v.x = *reinterpret_cast<uint32_t*>(&h0);
+                v.y = *reinterpret_cast<uint32_t*>(&h1);
+                v.z = *reinterpret_cast<uint32_t*>(&h2);
+                v.w = *reinterpret_cast<uint32_t*>(&h3);
+                *reinterpret_cast<uint4*>(dst + j) = v;
+              }
+            } else {
+              for (int j = 0; j < 32; ++j)
+                if (col + j < p.N) dst[j] = __float2bfloat16_rn(__uint_as_float(r[j]) * alpha);
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+}  // namespace bw

@@ -1,0 +1,336 @@
+// Device quantisers (the staging step in front of every GEMM) and small layout helpers.
+//
+// Element rules follow the reference bit for bit:
+//   fp16: __float2half round-to-nearest-even            (src/gemm_mma.cu:147-150)
+//   e4m3: __nv_fp8_e4m3(x), i.e. RNE with satfinite      (src/gemm_mma_fp8.cu:37-45)
+//   e2m1: f32_to_e2m1, first strictly-nearest level of {0,.5,1,1.5,2,3,4,6} by fabsf
+//         distance computed in fp32, sign bit iff v < 0   (src/gemm_mma_fp8.cu:47-58)
+//   fp4 byte container: code << 2 (kind::f8f6f4 alignment) (src/gemm_mma_fp8.cu:61-68)
+//   packed fp4: element 2i in the low nibble              (src/gemm_mma_fp8.cu:70-80)
+// New behaviour (no reference counterpart): per-tensor amax scaling and UE8M0 block-32
+// scales (e = floor(log2(block amax)) - 2).
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+
+#include "bw_runtime.cuh"
+
+namespace bw {
+namespace {
+
+constexpr int kQThreads = 256;
+
+__device__ __forceinline__ uint8_t e2m1_code(float v) {
+  const float lv[8] = {0.f, 0.5f, 1.f, 1.5f, 2.f, 3.f, 4.f, 6.f};
+  const float a = fabsf(v);
+  int best = 0;
+  float bd = fabsf(a - lv[0]);
+#pragma unroll
+  for (int i = 1; i < 8; ++i) {
+    const float d = fabsf(a - lv[i]);
+    if (d < bd) { bd = d; best = i; }
+  }
+  return static_cast<uint8_t>((v < 0.f ? 8 : 0) | best);
+}
+
+__device__ __forceinline__ uint8_t e4m3_sat(float x) {
+  return static_cast<uint8_t>(__nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3));
+}
+
+// ---------------------------------------------------------------- fp16
+__global__ void k_f32_to_f16(const float* __restrict__ src, __half* __restrict__ dst, long long n) {
+  const long long n4 = n / 4;
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n4; i += stride) {
+    const float4 v = reinterpret_cast<const float4*>(src)[i];
+    __half2 a = __floats2half2_rn(v.x, v.y), b = __floats2half2_rn(v.z, v.w);
+    uint2 o;
+    o.x = *reinterpret_cast<uint32_t*>(&a);
+    o.y = *reinterpret_cast<uint32_t*>(&b);
+    reinterpret_cast<uint2*>(dst)[i] = o;
+  }
+  for (long long i = n4 * 4 + blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n; i += stride)
+    dst[i] = __float2half_rn(src[i]);
+}
+
+// ---------------------------------------------------------------- amax
+__global__ void k_amax(const float* __restrict__ src, long long n, unsigned* __restrict__ out) {
+  float m = 0.f;
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n; i += stride)
+    m = fmaxf(m, fabsf(src[i]));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  __shared__ float wm[kQThreads / 32];
+  if ((threadIdx.x & 31) == 0) wm[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < kQThreads / 32; ++w) m = fmaxf(m, wm[w]);
+    atomicMax(out, __float_as_uint(m));  // non-negative floats order like their bits
+  }
+}
+
+// Per-tensor multiplier and the scale handed to the GEMM epilogue.
+//   NONE: q = cvt(x), s = 1. FIXED8: q = cvt(8x), s = 1/8. AMAX: q = cvt(x * (qmax/amax)),
+//   s = amax/qmax (amax == 0 -> 1).
+__device__ __forceinline__ void tensor_scale(int mode, const unsigned* amax_bits, float qmax, float& mul,
+                                             float& s) {
+  if (mode == BW_SCALE_FIXED8) { mul = 8.f; s = 0.125f; return; }
+  if (mode == BW_SCALE_AMAX) {
+    const float amax = __uint_as_float(*amax_bits);
+    if (amax > 0.f && amax < INFINITY) { mul = qmax / amax; s = amax / qmax; return; }
+  }
+  mul = 1.f;
+  s = 1.f;
+}
+
+// Quantise rows x cols fp32 into dst (rows x cols, or cols x rows when transposing).
+// FMT 0 = e4m3 byte, 1 = e2m1 byte container (<<2), 2 = e2m1 packed pairs.
+// Transposes go through a 32 x 33 shared tile so both sides stay coalesced.
+template <int FMT>
+__device__ __forceinline__ uint8_t encode(float x) {
+  if constexpr (FMT == 0) return e4m3_sat(x);
+  else return e2m1_code(x);
+}
+
+template <int FMT>
+__global__ void k_quant_rowmajor(const float* __restrict__ src, uint8_t* __restrict__ dst, int rows, int cols,
+                                 int mode, float qmax, const unsigned* amax_bits, float* scale_out) {
+  float mul, s;
+  tensor_scale(mode, amax_bits, qmax, mul, s);
+  if (scale_out && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) *scale_out = s;
+  const long long n = static_cast<long long>(rows) * cols;
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  if constexpr (FMT == 2) {
+    const long long npairs = n / 2;  // cols is even: pairs never straddle rows
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < npairs; i += stride) {
+      const float2 v = reinterpret_cast<const float2*>(src)[i];
+      dst[i] = static_cast<uint8_t>(e2m1_code(v.x * mul) | (e2m1_code(v.y * mul) << 4));
+    }
+  } else {
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n; i += stride) {
+      const uint8_t c = encode<FMT>(src[i] * mul);
+      dst[i] = (FMT == 1) ? static_cast<uint8_t>(c << 2) : c;
+    }
+  }
+}
+
+template <int FMT>
+__global__ void k_quant_transpose(const float* __restrict__ src, uint8_t* __restrict__ dst, int rows, int cols,
+                                  int mode, float qmax, const unsigned* amax_bits, float* scale_out) {
+  // src rows x cols -> dst cols x rows. Block handles a 64 (src rows) x 32 (src cols) tile.
+  __shared__ float tile[64][33];
+  float mul, s;
+  tensor_scale(mode, amax_bits, qmax, mul, s);
+  if (scale_out && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) *scale_out = s;
+  const int r0 = blockIdx.y * 64, c0 = blockIdx.x * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
+  for (int i = ty; i < 64; i += 8) {
+    const int r = r0 + i, c = c0 + tx;
+    tile[i][tx] = (r < rows && c < cols) ? src[static_cast<size_t>(r) * cols + c] * mul : 0.f;
+  }
+  __syncthreads();
+  if constexpr (FMT == 2) {
+    // dst row = src column c0 + j; 64 src rows -> 32 packed bytes per dst row.
+    for (int j = ty; j < 32; j += 8) {
+      const int c = c0 + j, r = r0 + 2 * tx;
+      if (c < cols && r < rows)
+        dst[static_cast<size_t>(c) * (rows / 2) + r / 2] =
+            static_cast<uint8_t>(e2m1_code(tile[2 * tx][j]) | (e2m1_code(tile[2 * tx + 1][j]) << 4));
+    }
+  } else {
+    for (int j = ty; j < 32; j += 8) {
+      const int c = c0 + j;
+      for (int h = 0; h < 2; ++h) {
+        const int i = tx + 32 * h, r = r0 + i;
+        if (c < cols && r < rows) {
+          const uint8_t code = encode<FMT>(tile[i][j]);
+          dst[static_cast<size_t>(c) * rows + r] = (FMT == 1) ? static_cast<uint8_t>(code << 2) : code;
+        }
+      }
+    }
+  }
+}
+
+// MXFP4: one thread per (outer index o, 32-element K block j).
+__global__ void k_quant_mx(const float* __restrict__ src, uint8_t* __restrict__ dst, uint8_t* __restrict__ sf,
+                           int outer, int K, int transpose, int src_cols, int mode) {
+  const int nkb = K / 32;
+  const long long total = static_cast<long long>(outer) * nkb;
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  const size_t kg = (static_cast<size_t>(nkb) + 3) / 4;
+  for (long long t = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; t < total; t += stride) {
+    // Transposed sources put consecutive threads on consecutive o (coalesced along src rows).
+    const int o = transpose ? static_cast<int>(t % outer) : static_cast<int>(t / nkb);
+    const int j = transpose ? static_cast<int>(t / outer) : static_cast<int>(t % nkb);
+    float v[32];
+    if (transpose) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = src[static_cast<size_t>(j * 32 + i) * src_cols + o];
+    } else {
+      const float4* p4 = reinterpret_cast<const float4*>(src + static_cast<size_t>(o) * K + j * 32);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 q = p4[i];
+        v[4 * i] = q.x; v[4 * i + 1] = q.y; v[4 * i + 2] = q.z; v[4 * i + 3] = q.w;
+      }
+    }
+    float mul = 8.f;
+    uint8_t byte = 127;
+    if (mode == BW_MX_BLOCK32) {
+      float amax = 0.f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+      // e = floor(log2(amax)) - 2 read from the exponent field; zero and subnormal blocks
+      // clamp to e = -127 (byte 0). Multiplier 2^-e is built from its exponent bits.
+      const int biased = static_cast<int>((__float_as_uint(amax) >> 23) & 0xFF);
+      int e = (biased == 0) ? -127 : biased - 127 - 2;
+      if (e < -127) e = -127;
+      if (e > 127) e = 127;
+      byte = static_cast<uint8_t>(e + 127);
+      const int mexp = 127 - e;  // exponent field of 2^-e, in [0, 254]
+      mul = (mexp >= 1) ? __uint_as_float(static_cast<uint32_t>(mexp) << 23) : 1.f;
+      if (e == -127) mul = __uint_as_float(254u << 23);  // 2^127
+    }
+    uint32_t w[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int i = 0; i < 32; ++i) w[i / 8] |= static_cast<uint32_t>(e2m1_code(v[i] * mul)) << (4 * (i % 8));
+    *reinterpret_cast<uint4*>(dst + static_cast<size_t>(o) * (K / 2) + j * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+    const int r = o % 128;
+    sf[((static_cast<size_t>(o) / 128) * kg + j / 4) * 512 + (r % 32) * 16 + (r / 32) * 4 + (j % 4)] = byte;
+  }
+}
+
+__global__ void k_unshard(const float* __restrict__ src, float* __restrict__ dst, int M, int N, int world) {
+  const int ns = N / world;
+  const long long total = static_cast<long long>(M) * N;
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total; i += stride) {
+    const long long m = i / N;
+    const int c = static_cast<int>(i % N);
+    const int r = c / ns, j = c % ns;
+    dst[i] = src[(static_cast<long long>(r) * M + m) * ns + j];
+  }
+}
+
+int grid_for(long long n, const DeviceState& d) {
+  long long g = (n + kQThreads - 1) / kQThreads;
+  const long long cap = static_cast<long long>(d.sms) * 16;
+  if (g > cap) g = cap;
+  if (g < 1) g = 1;
+  return static_cast<int>(g);
+}
+
+// Shared driver for the per-tensor quantisers (fp8 and fp4).
+template <int FMT>
+int quant_tensor(const float* src, uint8_t* dst, float* scale_out, int rows, int cols, int transpose, int mode,
+                 float qmax, cudaStream_t s) {
+  if (rows < 0 || cols < 0) return set_error(BW_ERR_INVALID, "negative size");
+  if (mode != BW_SCALE_NONE && mode != BW_SCALE_FIXED8 && mode != BW_SCALE_AMAX)
+    return set_error(BW_ERR_INVALID, "bad scale_mode %d", mode);
+  const long long n = static_cast<long long>(rows) * cols;
+  DeviceState* d;
+  int r = ensure_device(&d);
+  if (r != BW_OK) return r;
+  if (n == 0) {
+    if (scale_out) {
+      const float one = 1.f;
+      BW_CUDA(cudaMemcpyAsync(scale_out, &one, sizeof(float), cudaMemcpyHostToDevice, s));
+    }
+    return BW_OK;
+  }
+  if (!src || !dst) return set_error(BW_ERR_INVALID, "null src/dst");
+  if (FMT == 2 && ((transpose ? rows : cols) % 2 != 0))
+    return set_error(BW_ERR_INVALID, "packed fp4 needs an even contiguous dimension");
+  if (FMT == 2 && !transpose && (reinterpret_cast<uintptr_t>(src) & 7u))
+    return set_error(BW_ERR_INVALID, "packed fp4 source must be 8-byte aligned");
+  unsigned* amax = static_cast<unsigned*>(d->workspace);
+  if (mode == BW_SCALE_AMAX) {
+    BW_CUDA(cudaMemsetAsync(amax, 0, sizeof(unsigned), s));
+    k_amax<<<grid_for(n, *d), kQThreads, 0, s>>>(src, n, amax);
+    BW_CUDA(cudaGetLastError());
+  }
+  if (transpose) {
+    dim3 grid((cols + 31) / 32, (rows + 63) / 64);
+    k_quant_transpose<FMT><<<grid, kQThreads, 0, s>>>(src, dst, rows, cols, mode, qmax, amax, scale_out);
+  } else {
+    k_quant_rowmajor<FMT><<<grid_for(FMT == 2 ? n / 2 : n, *d), kQThreads, 0, s>>>(src, dst, rows, cols, mode, qmax,
+                                                                                  amax, scale_out);
+  }
+  BW_CUDA(cudaGetLastError());
+  return BW_OK;
+}
+
+}  // namespace
+}  // namespace bw
+
+using namespace bw;
+
+extern "C" {
+
+int bw_quantize_f16(const float* src, void* dst, long long n, void* stream) {
+  if (n < 0) return set_error(BW_ERR_INVALID, "negative n");
+  if (n == 0) return BW_OK;
+  if (!src || !dst) return set_error(BW_ERR_INVALID, "null src/dst");
+  if (!aligned16(src) || (reinterpret_cast<uintptr_t>(dst) & 7u))
+    return set_error(BW_ERR_INVALID, "src must be 16-byte and dst 8-byte aligned");
+  DeviceState* d;
+  int r = ensure_device(&d);
+  if (r != BW_OK) return r;
+  k_f32_to_f16<<<grid_for(n / 4 + 1, *d), kQThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      src, static_cast<__half*>(dst), n);
+  BW_CUDA(cudaGetLastError());
+  return BW_OK;
+}
+
+int bw_quantize_fp8(const float* src, uint8_t* dst, float* scale_out, int rows, int cols, int transpose,
+                    int scale_mode, void* stream) {
+  return quant_tensor<0>(src, dst, scale_out, rows, cols, transpose, scale_mode, 448.f,
+                         static_cast<cudaStream_t>(stream));
+}
+
+int bw_quantize_fp4(const float* src, uint8_t* dst, float* scale_out, int rows, int cols, int transpose,
+                    int scale_mode, int container, void* stream) {
+  if (container == BW_FP4_PACKED)
+    return quant_tensor<2>(src, dst, scale_out, rows, cols, transpose, scale_mode, 6.f,
+                           static_cast<cudaStream_t>(stream));
+  if (container == BW_FP4_BYTE_SHL2)
+    return quant_tensor<1>(src, dst, scale_out, rows, cols, transpose, scale_mode, 6.f,
+                           static_cast<cudaStream_t>(stream));
+  return set_error(BW_ERR_INVALID, "bad fp4 container %d", container);
+}
+
+int bw_quantize_mxfp4(const float* src, uint8_t* dst, uint8_t* sf, int rows, int cols, int transpose, int mode,
+                      void* stream) {
+  if (rows < 0 || cols < 0) return set_error(BW_ERR_INVALID, "negative size");
+  if (mode != BW_MX_UNIT_FIXED8 && mode != BW_MX_BLOCK32) return set_error(BW_ERR_INVALID, "bad mx mode %d", mode);
+  const int K = transpose ? rows : cols;
+  const int outer = transpose ? cols : rows;
+  if (K % 32 != 0) return set_error(BW_ERR_INVALID, "mxfp4 needs K %% 32 == 0 (got %d)", K);
+  if (static_cast<long long>(rows) * cols == 0) return BW_OK;
+  if (!src || !dst || !sf) return set_error(BW_ERR_INVALID, "null src/dst/sf");
+  if (!aligned16(src) || !aligned16(dst)) return set_error(BW_ERR_INVALID, "src and dst must be 16-byte aligned");
+  DeviceState* d;
+  int r = ensure_device(&d);
+  if (r != BW_OK) return r;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  BW_CUDA(cudaMemsetAsync(sf, 0x7f, bw_sf_bytes(outer, K), s));
+  const long long total = static_cast<long long>(outer) * (K / 32);
+  k_quant_mx<<<grid_for(total, *d), kQThreads, 0, s>>>(src, dst, sf, outer, K, transpose, cols, mode);
+  BW_CUDA(cudaGetLastError());
+  return BW_OK;
+}
+
+int bw_unshard_columns(const float* C_shardmajor, float* C_rowmajor, int M, int N, int world, void* stream) {
+  if (M < 0 || N < 0 || world <= 0 || N % world != 0) return set_error(BW_ERR_INVALID, "bad unshard shape");
+  if (static_cast<long long>(M) * N == 0) return BW_OK;
+  if (!C_shardmajor || !C_rowmajor) return set_error(BW_ERR_INVALID, "null buffer");
+  DeviceState* d;
+  int r = ensure_device(&d);
+  if (r != BW_OK) return r;
+  k_unshard<<<grid_for(static_cast<long long>(M) * N, *d), kQThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      C_shardmajor, C_rowmajor, M, N, world);
+  BW_CUDA(cudaGetLastError());
+  return BW_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,169 @@
+// Library runtime: device state, error reporting, TMA descriptor encoding.
+// The reference reports errors by printing and exit(1) (include/util.cuh:7-8); here every
+// failure becomes a status code plus a per-thread message (bw_last_error_string).
+#include <cudaTypedefs.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <mutex>
+
+#include "bw_runtime.cuh"
+
+namespace bw {
+
+namespace {
+thread_local std::string g_err;
+constexpr int kMaxDevices = 64;
+DeviceState g_dev[kMaxDevices];
+std::mutex g_mu;
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+unsigned long long g_budget_ns = 2000000000ull;
+bool g_budget_from_env = false;
+}  // namespace
+
+int set_error(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+int cuda_error(cudaError_t e, const char* what) {
+  return set_error(BW_ERR_CUDA, "%s failed: %s", what, cudaGetErrorString(e));
+}
+
+unsigned long long wait_budget_ns() {
+  if (!g_budget_from_env) {
+    g_budget_from_env = true;
+    if (const char* s = getenv("BW_WAIT_BUDGET_MS")) {
+      long long ms = atoll(s);
+      if (ms > 0) g_budget_ns = static_cast<unsigned long long>(ms) * 1000000ull;
+    }
+  }
+  return g_budget_ns;
+}
+
+static int load_encode() {
+  if (g_encode) return BW_OK;
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  cudaError_t e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q);
+  if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
+    return set_error(BW_ERR_CUDA, "cannot resolve cuTensorMapEncodeTiled from the driver");
+  g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  return BW_OK;
+}
+
+int ensure_device(DeviceState** out) {
+  int dev = 0;
+  BW_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return set_error(BW_ERR_INVALID, "device index %d out of range", dev);
+  DeviceState& d = g_dev[dev];
+  if (!d.ready) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!d.ready) {
+      cudaDeviceProp prop;
+      BW_CUDA(cudaGetDeviceProperties(&prop, dev));
+      if (prop.major != 10 || prop.minor != 0)
+        return set_error(BW_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a", dev,
+                         prop.major, prop.minor);
+      int r = load_encode();
+      if (r != BW_OK) return r;
+      d.sms = prop.multiProcessorCount;
+      d.major = prop.major;
+      d.minor = prop.minor;
+      BW_CUDA(cudaMalloc(&d.status, sizeof(int)));
+      BW_CUDA(cudaMemset(d.status, 0, sizeof(int)));
+      d.workspace_bytes = 4096;
+      BW_CUDA(cudaMalloc(&d.workspace, d.workspace_bytes));
+      BW_CUDA(cudaMemset(d.workspace, 0, d.workspace_bytes));
+      d.ready = true;
+    }
+  }
+  *out = &d;
+  return BW_OK;
+}
+
+int make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner, uint64_t outer,
+                 uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer) {
+  int r = load_encode();
+  if (r != BW_OK) return r;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult cr = g_encode(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (cr != CUDA_SUCCESS)
+    return set_error(BW_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d): dims %llu x %llu stride %llu box %u x %u",
+                     static_cast<int>(cr), (unsigned long long)inner, (unsigned long long)outer,
+                     (unsigned long long)row_stride_bytes, box_inner, box_outer);
+  return BW_OK;
+}
+
+}  // namespace bw
+
+using namespace bw;
+
+extern "C" {
+
+const char* bw_last_error_string(void) { return g_err.c_str(); }
+
+int bw_version(void) { return (0 << 16) | 3; }
+
+int bw_init(int device) {
+  BW_CUDA(cudaSetDevice(device));
+  DeviceState* d;
+  return ensure_device(&d);
+}
+
+int bw_num_sms(int device) {
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return -1;
+  return n;
+}
+
+int bw_shutdown(void) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  int cur = 0;
+  cudaGetDevice(&cur);
+  for (int i = 0; i < kMaxDevices; ++i) {
+    DeviceState& d = g_dev[i];
+    if (!d.ready) continue;
+    cudaSetDevice(i);
+    cudaFree(d.status);
+    cudaFree(d.workspace);
+    d = DeviceState{};
+  }
+  cudaSetDevice(cur);
+  return BW_OK;
+}
+
+int bw_device_status(void* stream, int* out_status) {
+  if (!out_status) return set_error(BW_ERR_INVALID, "out_status is null");
+  DeviceState* d;
+  int r = ensure_device(&d);
+  if (r != BW_OK) return r;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  BW_CUDA(cudaStreamSynchronize(s));
+  int v = 0;
+  BW_CUDA(cudaMemcpy(&v, d->status, sizeof(int), cudaMemcpyDeviceToHost));
+  BW_CUDA(cudaMemset(d->status, 0, sizeof(int)));
+  *out_status = v;
+  if (v != 0) return set_error(BW_ERR_TIMEOUT, "kernel wait budget expired at site %d", v & 255);
+  return BW_OK;
+}
+
+int bw_set_wait_budget_ns(unsigned long long ns) {
+  if (ns == 0) return set_error(BW_ERR_INVALID, "wait budget must be > 0");
+  wait_budget_ns();
+  g_budget_ns = ns;
+  return BW_OK;
+}
+
+}  // extern "C"

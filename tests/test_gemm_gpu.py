@@ -1,0 +1,251 @@
+"""GPU parity: the tcgen05 GEMMs and device quantisers (through the C ABI) against the oracle.
+
+Tolerances are the north star's:
+  FP16:          max|C - C_ref| <= 2^-10 * sqrt(K) * max|a| * max|b|
+  FP8/FP4/MXFP4: max|C - C_ref| <= 1e-5 * K * max|a_deq| * max|b_deq|  (+ 2^-8 |C_ref| for BF16 out)
+where C_ref is the FP64 oracle GEMM over the identically quantised inputs. Quantisers are
+bit-exact. Full-size (8192) shapes are checked through exactly representable inputs
+(small integers: FP32 accumulation is exact) on sampled rows and columns.
+"""
+import numpy as np
+import pytest
+
+import bwgemm
+import oracle as o
+
+pytestmark = pytest.mark.gpu
+
+
+def _t(x, dev):
+    import torch
+
+    return torch.from_numpy(np.ascontiguousarray(x)).to(dev)
+
+
+def _np(t):
+    import torch
+
+    if t.dtype == torch.bfloat16:
+        t = t.float()
+    return t.cpu().numpy()
+
+
+def _f16(x):
+    return o.f16_to_f32(o.f32_to_f16(x))
+
+
+def _status_ok():
+    assert bwgemm.device_status() == 0
+
+
+F16_SHAPES = [(256, 256, 256), (1024, 1024, 1024), (129, 136, 72), (128, 8, 8), (1, 8, 64), (300, 520, 1000),
+              (640, 1280, 2048), (4096, 256, 64)]
+
+
+@pytest.mark.parametrize("M,N,K", F16_SHAPES)
+@pytest.mark.parametrize("b_transposed", [False, True])
+def test_f16_parity(cuda_dev, M, N, K, b_transposed):
+    import torch
+
+    A = _f16(o.seeded_uniform((M, K), 1))
+    B = _f16(o.seeded_uniform((K, N), 2))
+    Bdev = B.T.copy() if b_transposed else B
+    C = bwgemm.gemm_f16(_t(A, cuda_dev).half(), _t(Bdev, cuda_dev).half(), b_transposed=b_transposed)
+    torch.cuda.synchronize()
+    _status_ok()
+    R = o.gemm_f64(A, B)
+    err = np.abs(_np(C) - R).max()
+    tol = o.f16_tolerance(K, np.abs(A).max(), np.abs(B).max())
+    assert err <= tol, (err, tol)
+
+
+def test_f16_k_zero_and_empty(cuda_dev):
+    import torch
+
+    A = torch.zeros((64, 0), dtype=torch.float16, device=cuda_dev)
+    B = torch.zeros((0, 64), dtype=torch.float16, device=cuda_dev)
+    C = torch.full((64, 64), 7.0, device=cuda_dev)
+    bwgemm.gemm_f16(A, B, C)
+    assert float(C.abs().max()) == 0.0
+    E = torch.empty((0, 64), dtype=torch.float32, device=cuda_dev)
+    bwgemm.gemm_f16(torch.empty((0, 64), dtype=torch.float16, device=cuda_dev),
+                    torch.empty((64, 64), dtype=torch.float16, device=cuda_dev), E)
+
+
+def test_f16_rejects_bad_shapes(cuda_dev):
+    import torch
+
+    A = torch.zeros((64, 12), dtype=torch.float16, device=cuda_dev)
+    B = torch.zeros((12, 64), dtype=torch.float16, device=cuda_dev)
+    with pytest.raises(bwgemm.BwError) as e:
+        bwgemm.gemm_f16(A, B)
+    assert e.value.code == bwgemm.BW_ERR_INVALID
+
+
+def _exact_ints(shape, seed, lo=-2, hi=2):
+    return np.random.default_rng(seed).integers(lo, hi + 1, size=shape).astype(np.float32)
+
+
+@pytest.mark.parametrize("M,N,K", [(8192, 8192, 8192), (16384, 2048, 8192), (128, 65536, 8192)])
+def test_f16_full_size_exact(cuda_dev, M, N, K):
+    """Integer inputs in [-2, 2]: every partial sum is exact in FP32, so the GPU result must
+    equal the FP64 oracle bit for bit on the sampled rows and columns."""
+    import torch
+
+    A = _exact_ints((M, K), 11)
+    B = _exact_ints((K, N), 12)
+    C = _np(bwgemm.gemm_f16(_t(A, cuda_dev).half(), _t(B, cuda_dev).half()))
+    torch.cuda.synchronize()
+    _status_ok()
+    rng = np.random.default_rng(3)
+    rows = np.unique(np.concatenate([rng.integers(0, M, 48), [0, M - 1]]))
+    cols = np.unique(np.concatenate([rng.integers(0, N, 48), [0, N - 1]]))
+    Rr = o.gemm_f64(A[rows], B)
+    assert np.array_equal(C[rows].astype(np.float64), Rr)
+    Rc = o.gemm_f64(A, np.ascontiguousarray(B[:, cols]))
+    assert np.array_equal(C[:, cols].astype(np.float64), Rc)
+
+
+def test_f16_linearity_full_size(cuda_dev):
+    """C(A, B1 + B2) == C(A, B1) + C(A, B2) on exactly representable inputs at 8192^3."""
+    import torch
+
+    M = N = K = 8192
+    A = _t(_exact_ints((M, K), 21), cuda_dev).half()
+    B1 = _t(_exact_ints((K, N), 22, -1, 1), cuda_dev).half()
+    B2 = _t(_exact_ints((K, N), 23, -1, 1), cuda_dev).half()
+    C12 = bwgemm.gemm_f16(A, (B1 + B2).contiguous())
+    C1 = bwgemm.gemm_f16(A, B1)
+    C2 = bwgemm.gemm_f16(A, B2)
+    torch.cuda.synchronize()
+    assert torch.equal(C12, C1 + C2)
+
+
+# ------------------------------------------------------------------ quantisers
+def test_quantisers_match_golden(cuda_dev):
+    g = np.load(__import__("os").path.join(__import__("os").path.dirname(__file__), "golden", "quant_golden.npz"))
+    x = _t(g["x"], cuda_dev)
+    q, s = bwgemm.quantize_fp8(x, False, bwgemm.SCALE_NONE)
+    assert np.array_equal(_np(q), g["fp8"])
+    q, s = bwgemm.quantize_fp4(x, False, bwgemm.SCALE_FIXED8, bwgemm.FP4_BYTE_SHL2)
+    assert np.array_equal(_np(q), g["fp4_byte"])
+    q, sf = bwgemm.quantize_mxfp4(x, False, bwgemm.MX_UNIT_FIXED8)
+    assert np.array_equal(_np(q), g["mxfp4_ref"])
+    q, sf = bwgemm.quantize_mxfp4(x, False, bwgemm.MX_BLOCK32)
+    assert np.array_equal(_np(q), g["mxfp4_q"])
+    assert np.array_equal(_np(sf), g["mxfp4_sf"])
+    h = bwgemm.quantize_f16(x)
+    assert np.array_equal(_np(h.view(__import__("torch").int16)).view(np.uint16), g["f16"])
+
+
+@pytest.mark.parametrize("transpose", [False, True])
+@pytest.mark.parametrize("mode", [bwgemm.SCALE_NONE, bwgemm.SCALE_FIXED8, bwgemm.SCALE_AMAX])
+def test_quantize_fp8_bit_exact(cuda_dev, transpose, mode):
+    x = o.seeded_normal((200, 328), 5) * 3
+    q, s = bwgemm.quantize_fp8(_t(x, cuda_dev), transpose, mode)
+    qr, sr = o.quant_fp8(x, transpose, mode)
+    assert np.array_equal(_np(q), qr)
+    assert float(_np(s)[0]) == sr
+
+
+@pytest.mark.parametrize("transpose", [False, True])
+@pytest.mark.parametrize("container", [bwgemm.FP4_PACKED, bwgemm.FP4_BYTE_SHL2])
+@pytest.mark.parametrize("mode", [bwgemm.SCALE_FIXED8, bwgemm.SCALE_AMAX])
+def test_quantize_fp4_bit_exact(cuda_dev, transpose, container, mode):
+    x = o.seeded_normal((192, 256), 6)
+    q, s = bwgemm.quantize_fp4(_t(x, cuda_dev), transpose, mode, container)
+    qr, sr = o.quant_fp4(x, transpose, mode, container)
+    assert np.array_equal(_np(q), qr)
+    assert float(_np(s)[0]) == sr
+
+
+@pytest.mark.parametrize("transpose", [False, True])
+@pytest.mark.parametrize("mode", [bwgemm.MX_UNIT_FIXED8, bwgemm.MX_BLOCK32])
+def test_quantize_mxfp4_bit_exact(cuda_dev, transpose, mode):
+    x = o.seeded_normal((256, 320), 7)
+    x[:, :7] *= 1e3
+    q, sf = bwgemm.quantize_mxfp4(_t(x, cuda_dev), transpose, mode)
+    qr, sfr = o.quant_mxfp4(x, transpose, mode)
+    assert np.array_equal(_np(q), qr)
+    assert np.array_equal(_np(sf), sfr)
+
+
+# ------------------------------------------------------------------ low-precision GEMMs
+LOWP_SHAPES = [(256, 256, 256), (1024, 1024, 1024), (129, 136, 96), (384, 640, 2048), (128, 8, 64)]
+
+
+@pytest.mark.parametrize("M,N,K", LOWP_SHAPES)
+@pytest.mark.parametrize("out", [bwgemm.OUT_F32, bwgemm.OUT_BF16])
+def test_fp8_parity(cuda_dev, M, N, K, out):
+    import torch
+
+    if K % 16:
+        pytest.skip("fp8 needs K % 16 == 0")
+    A = o.seeded_normal((M, K), 31)
+    B = o.seeded_normal((K, N), 32)
+    qa, sa = bwgemm.quantize_fp8(_t(A, cuda_dev), False, bwgemm.SCALE_AMAX)
+    qb, sb = bwgemm.quantize_fp8(_t(B, cuda_dev), True, bwgemm.SCALE_AMAX)
+    C = _np(bwgemm.gemm_fp8(qa, qb, sa, sb, out_dtype=out))
+    torch.cuda.synchronize()
+    _status_ok()
+    ra, rsa = o.quant_fp8(A, False, o.SCALE_AMAX)
+    rb, rsb = o.quant_fp8(B, True, o.SCALE_AMAX)
+    da = o.dequant_fp8(ra) * np.float32(rsa)
+    db = o.dequant_fp8(rb) * np.float32(rsb)
+    R = o.gemm_f64(o.dequant_fp8(ra), o.dequant_fp8(rb), b_trans=True) * (np.float64(np.float32(rsa * rsb)))
+    tol = o.lowp_tolerance(K, np.abs(da).max(), np.abs(db).max(), np.abs(R).max(), out == bwgemm.OUT_BF16)
+    err = np.abs(C - R).max()
+    assert err <= tol, (err, tol)
+
+
+@pytest.mark.parametrize("M,N,K", LOWP_SHAPES)
+def test_mxfp4_parity(cuda_dev, M, N, K):
+    import torch
+
+    A = o.seeded_normal((M, K), 41)
+    B = o.seeded_normal((K, N), 42)
+    qa, sfa = bwgemm.quantize_mxfp4(_t(A, cuda_dev), False, bwgemm.MX_BLOCK32)
+    qb, sfb = bwgemm.quantize_mxfp4(_t(B, cuda_dev), True, bwgemm.MX_BLOCK32)
+    C = _np(bwgemm.gemm_mxfp4(qa, qb, sfa, sfb, K, out_dtype=bwgemm.OUT_F32))
+    torch.cuda.synchronize()
+    _status_ok()
+    ra, rsfa = o.quant_mxfp4(A, False, o.MX_BLOCK32)
+    rb, rsfb = o.quant_mxfp4(B, True, o.MX_BLOCK32)
+    da = o.dequant_mxfp4(ra, rsfa, K)
+    db = o.dequant_mxfp4(rb, rsfb, K)
+    R = o.gemm_f64(da, db, b_trans=True)
+    tol = o.lowp_tolerance(K, np.abs(da).max(), np.abs(db).max())
+    err = np.abs(C - R).max()
+    assert err <= tol, (err, tol)
+
+
+@pytest.mark.parametrize("M,N,K", LOWP_SHAPES)
+def test_fp4_per_tensor_parity(cuda_dev, M, N, K):
+    import torch
+
+    A = o.seeded_normal((M, K), 51)
+    B = o.seeded_normal((K, N), 52)
+    qa, sa = bwgemm.quantize_fp4(_t(A, cuda_dev), False, bwgemm.SCALE_AMAX, bwgemm.FP4_PACKED)
+    qb, sb = bwgemm.quantize_fp4(_t(B, cuda_dev), True, bwgemm.SCALE_AMAX, bwgemm.FP4_PACKED)
+    C = _np(bwgemm.gemm_fp4(qa, qb, K, sa, sb, out_dtype=bwgemm.OUT_BF16))
+    torch.cuda.synchronize()
+    _status_ok()
+    ra, rsa = o.quant_fp4(A, False, o.SCALE_AMAX, o.FP4_PACKED)
+    rb, rsb = o.quant_fp4(B, True, o.SCALE_AMAX, o.FP4_PACKED)
+    da = o.dequant_mxfp4(ra, None, K)
+    db = o.dequant_mxfp4(rb, None, K)
+    R = o.gemm_f64(da, db, b_trans=True) * np.float64(np.float32(rsa) * np.float32(rsb))
+    tol = o.lowp_tolerance(K, np.abs(da).max() * rsa, np.abs(db).max() * rsb, np.abs(R).max(), True)
+    err = np.abs(C - R).max()
+    assert err <= tol, (err, tol)
+
+
+def test_unshard_columns(cuda_dev):
+    import torch
+
+    M, N, world = 64, 96, 4
+    full = o.seeded_uniform((M, N), 9)
+    shards = np.stack([full[:, r * (N // world):(r + 1) * (N // world)] for r in range(world)])
+    out = bwgemm.unshard_columns(_t(np.ascontiguousarray(shards), cuda_dev), M, N, world)
+    torch.cuda.synchronize()
+    assert np.array_equal(_np(out), full)
