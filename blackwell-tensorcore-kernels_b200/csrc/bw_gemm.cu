@@ -3,6 +3,7 @@
 #include <cstdlib>
 
 #include "bw_gemm_kernel.cuh"
+#include "bw_gemm_pair.cuh"
 #include "bw_runtime.cuh"
 
 namespace bw {
@@ -15,7 +16,8 @@ int env_int(const char* name, int dflt) {
 }
 
 template <Kind KIND, bool B_MN, int BN, int STAGES, int ACC_BUFS, Out OUT>
-int launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p, cudaStream_t stream, const DeviceState& d) {
+int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, GemmParams p, cudaStream_t stream,
+           const DeviceState& d) {
   using Cfg = GemmCfg<KIND, B_MN, BN, STAGES, ACC_BUFS>;
   auto kern = bw_tc_gemm_kernel<KIND, B_MN, BN, STAGES, ACC_BUFS, OUT>;
   static bool attr_done[64] = {};
@@ -29,9 +31,69 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p, cudaStrea
   int grid = tiles < d.sms ? tiles : d.sms;
   const int cap = env_int("BW_MAX_CTAS", 0);
   if (cap > 0 && grid > cap) grid = cap;
-  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, p);
+  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, tc, p);
   BW_CUDA(cudaGetLastError());
   return BW_OK;
+}
+
+template <Kind KIND, bool B_MN, int STAGES, Out OUT>
+int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, GemmParams p,
+                cudaStream_t stream, const DeviceState& d) {
+  using Cfg = PairCfg<KIND, STAGES>;
+  auto kern = bw_tc_gemm_pair_kernel<KIND, B_MN, STAGES, OUT>;
+  static bool attr_done[64] = {};
+  int dev = 0;
+  BW_CUDA(cudaGetDevice(&dev));
+  if (!attr_done[dev & 63]) {
+    BW_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
+    attr_done[dev & 63] = true;
+  }
+  // Persistent grid: as many CTA pairs as can be co-resident (clusters must sit inside one
+  // GPC, so this can be below sms/2).
+  static int max_clusters[64] = {};
+  if (max_clusters[dev & 63] == 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (d.sms / 2), 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = d.sms / 2;
+    }
+    max_clusters[dev & 63] = n;
+  }
+  const int tiles = ((p.M + 255) / 256) * ((p.N + 255) / 256);
+  const int resident = max_clusters[dev & 63];
+  int clusters = tiles < resident ? tiles : resident;
+  const int cap = env_int("BW_MAX_CTAS", 0);
+  if (cap > 1 && clusters > cap / 2) clusters = cap / 2;
+  kern<<<2 * clusters, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, tc, p);
+  BW_CUDA(cudaGetLastError());
+  return BW_OK;
+}
+
+// CTA pairs (256 x 256 tiles) when the problem fills at least most of the SM pairs.
+bool use_pair(int M, int N, const DeviceState& d) {
+  const int forced = env_int("BW_PAIR", -1);
+  if (forced == 0) return false;
+  if (forced == 1) return true;
+  const long tiles = static_cast<long>((M + 255) / 256) * ((N + 255) / 256);
+  return tiles >= d.sms / 2;
+}
+
+// Output tensor map for the TMA-store epilogue: 32 rows x 128 B boxes, 128B swizzle.
+int make_c_map(CUtensorMap* tc, void* C, int M, int N, int out_dtype) {
+  if (out_dtype == BW_OUT_BF16)
+    return make_tmap_2d(tc, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, C, N, M, uint64_t(N) * 2, 64, 32);
+  return make_tmap_2d(tc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, C, N, M, uint64_t(N) * 4, 32, 32);
 }
 
 GemmParams base_params(const DeviceState& d, void* C, int M, int N, int K) {
@@ -75,20 +137,30 @@ int gemm_f16_impl(const void* A, const void* B, float* C, int M, int N, int K, c
   DeviceState* d;
   if ((r = ensure_device(&d)) != BW_OK) return r;
   if (K == 0) { BW_CUDA(cudaMemsetAsync(C, 0, sizeof(float) * size_t(M) * N, s)); return BW_OK; }
-  const bool narrow = use_narrow(M, N, *d);
-  const int bn = narrow ? 128 : 256;
+  const bool pair = use_pair(M, N, *d);
+  const bool narrow = !pair && use_narrow(M, N, *d);
+  const int bn = pair ? 128 : narrow ? 128 : 256;
   CUtensorMap ta, tb;
   if ((r = make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, A, K, M, uint64_t(K) * 2, 64, 128)) != BW_OK) return r;
   if (b_mn) r = make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, B, N, K, uint64_t(N) * 2, 64, 64);
   else r = make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, B, K, N, uint64_t(K) * 2, 64, bn);
   if (r != BW_OK) return r;
+  CUtensorMap tc;
+  if ((r = make_c_map(&tc, C, M, N, BW_OUT_F32)) != BW_OK) return r;
   GemmParams p = base_params(*d, C, M, N, K);
-  if (b_mn) {
-    if (narrow) return launch<Kind::F16, true, 128, 6, 2, Out::F32>(ta, tb, p, s, *d);
-    return launch<Kind::F16, true, 256, 4, 2, Out::F32>(ta, tb, p, s, *d);
+  if (pair) {
+    const int st = env_int("BW_STAGES", 6);
+    if (b_mn && st == 4) return launch_pair<Kind::F16, true, 4, Out::F32>(ta, tb, tc, p, s, *d);
+    if (b_mn && st == 5) return launch_pair<Kind::F16, true, 5, Out::F32>(ta, tb, tc, p, s, *d);
+    if (b_mn) return launch_pair<Kind::F16, true, 6, Out::F32>(ta, tb, tc, p, s, *d);
+    return launch_pair<Kind::F16, false, 6, Out::F32>(ta, tb, tc, p, s, *d);
   }
-  if (narrow) return launch<Kind::F16, false, 128, 6, 2, Out::F32>(ta, tb, p, s, *d);
-  return launch<Kind::F16, false, 256, 4, 2, Out::F32>(ta, tb, p, s, *d);
+  if (b_mn) {
+    if (narrow) return launch<Kind::F16, true, 128, 6, 2, Out::F32>(ta, tb, tc, p, s, *d);
+    return launch<Kind::F16, true, 256, 4, 2, Out::F32>(ta, tb, tc, p, s, *d);
+  }
+  if (narrow) return launch<Kind::F16, false, 128, 6, 2, Out::F32>(ta, tb, tc, p, s, *d);
+  return launch<Kind::F16, false, 256, 4, 2, Out::F32>(ta, tb, tc, p, s, *d);
 }
 
 size_t out_elem_bytes(int out_dtype) { return out_dtype == BW_OUT_BF16 ? 2 : 4; }
@@ -103,20 +175,27 @@ int gemm_fp8_impl(const uint8_t* A, const uint8_t* Bt, const float* sa, const fl
   DeviceState* d;
   if ((r = ensure_device(&d)) != BW_OK) return r;
   if (K == 0) { BW_CUDA(cudaMemsetAsync(C, 0, out_elem_bytes(out_dtype) * size_t(M) * N, s)); return BW_OK; }
-  const bool narrow = use_narrow(M, N, *d);
-  const int bn = narrow ? 128 : 256;
+  const bool pair = use_pair(M, N, *d);
+  const bool narrow = !pair && use_narrow(M, N, *d);
+  const int bn = pair ? 128 : narrow ? 128 : 256;
   CUtensorMap ta, tb;
   if ((r = make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, A, K, M, uint64_t(K), 128, 128)) != BW_OK) return r;
   if ((r = make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, Bt, K, N, uint64_t(K), 128, bn)) != BW_OK) return r;
+  CUtensorMap tc;
+  if ((r = make_c_map(&tc, C, M, N, out_dtype)) != BW_OK) return r;
   GemmParams p = base_params(*d, C, M, N, K);
   p.scale_a = sa;
   p.scale_b = sb;
-  if (out_dtype == BW_OUT_F32) {
-    if (narrow) return launch<Kind::F8, false, 128, 6, 2, Out::F32>(ta, tb, p, s, *d);
-    return launch<Kind::F8, false, 256, 4, 2, Out::F32>(ta, tb, p, s, *d);
+  if (pair) {
+    if (out_dtype == BW_OUT_F32) return launch_pair<Kind::F8, false, 6, Out::F32>(ta, tb, tc, p, s, *d);
+    return launch_pair<Kind::F8, false, 6, Out::BF16>(ta, tb, tc, p, s, *d);
   }
-  if (narrow) return launch<Kind::F8, false, 128, 6, 2, Out::BF16>(ta, tb, p, s, *d);
-  return launch<Kind::F8, false, 256, 4, 2, Out::BF16>(ta, tb, p, s, *d);
+  if (out_dtype == BW_OUT_F32) {
+    if (narrow) return launch<Kind::F8, false, 128, 6, 2, Out::F32>(ta, tb, tc, p, s, *d);
+    return launch<Kind::F8, false, 256, 4, 2, Out::F32>(ta, tb, tc, p, s, *d);
+  }
+  if (narrow) return launch<Kind::F8, false, 128, 6, 2, Out::BF16>(ta, tb, tc, p, s, *d);
+  return launch<Kind::F8, false, 256, 4, 2, Out::BF16>(ta, tb, tc, p, s, *d);
 }
 
 int gemm_mxf4_impl(const uint8_t* A, const uint8_t* Bt, const uint8_t* sfa, const uint8_t* sfb, const float* sa,
@@ -135,14 +214,16 @@ int gemm_mxf4_impl(const uint8_t* A, const uint8_t* Bt, const uint8_t* sfa, cons
   CUtensorMap ta, tb;
   if ((r = make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, A, K / 2, M, uint64_t(K / 2), 128, 128)) != BW_OK) return r;
   if ((r = make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, Bt, K / 2, N, uint64_t(K / 2), 128, 128)) != BW_OK) return r;
+  CUtensorMap tc;
+  if ((r = make_c_map(&tc, C, M, N, out_dtype)) != BW_OK) return r;
   GemmParams p = base_params(*d, C, M, N, K);
   p.scale_a = sa;
   p.scale_b = sb;
   p.sfa = sfa;
   p.sfb = sfb;
   p.sf_kgroups = ((K + 31) / 32 + 3) / 4;
-  if (out_dtype == BW_OUT_F32) return launch<Kind::MXF4, false, 128, 6, 2, Out::F32>(ta, tb, p, s, *d);
-  return launch<Kind::MXF4, false, 128, 6, 2, Out::BF16>(ta, tb, p, s, *d);
+  if (out_dtype == BW_OUT_F32) return launch<Kind::MXF4, false, 128, 5, 2, Out::F32>(ta, tb, tc, p, s, *d);
+  return launch<Kind::MXF4, false, 128, 5, 2, Out::BF16>(ta, tb, tc, p, s, *d);
 }
 
 }  // namespace

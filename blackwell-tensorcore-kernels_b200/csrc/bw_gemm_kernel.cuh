@@ -35,22 +35,27 @@ constexpr int kBM = 128;          // rows of A per tile (one TMEM lane per row)
 constexpr int kSlabBytes = 128;   // bytes of K per k-slab row (one 128B swizzle atom)
 constexpr int kThreads = 192;     // 6 warps
 constexpr int kEpiWarps = 4;
+constexpr int kEpiBufBytes = 32 * 128;                   // per-warp staging buffer: 32 rows x 128 B
+constexpr int kEpiBytes = kEpiWarps * 2 * kEpiBufBytes;  // two buffers per epilogue warp: 32 KB
 
 template <Kind KIND>
 struct KindTraits;
 template <>
 struct KindTraits<Kind::F16> {
   static constexpr int kElemsPerSlab = 64;  // 64 fp16 = 128 B
+  static constexpr int kCoordPerSlab = 64;  // tensor-map units (elements) per slab
   static constexpr uint32_t kFmt = 0;       // F16
 };
 template <>
 struct KindTraits<Kind::F8> {
   static constexpr int kElemsPerSlab = 128;  // 128 e4m3
+  static constexpr int kCoordPerSlab = 128;
   static constexpr uint32_t kFmt = 0;        // E4M3
 };
 template <>
 struct KindTraits<Kind::MXF4> {
   static constexpr int kElemsPerSlab = 256;  // 256 packed e2m1 = 128 B
+  static constexpr int kCoordPerSlab = 128;  // the tensor map counts packed bytes
   static constexpr uint32_t kFmt = 1;
 };
 
@@ -84,10 +89,12 @@ struct GemmCfg {
   static_assert(kNeedCols <= 512, "TMEM budget exceeded");
   static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN");
   static_assert(KIND != Kind::MXF4 || BN % 128 == 0, "MXF4 tiles cover whole 128-row SF blocks");
-  static constexpr int kBarOffset = STAGES * kStageBytes;
+  static constexpr int kEpiOffset = STAGES * kStageBytes;
+  static constexpr int kBarOffset = kEpiOffset + kEpiBytes;
   // full[S], empty[S], accfull[ACC], accempty[ACC], teardown
   static constexpr int kNumBars = 2 * STAGES + 2 * ACC_BUFS + 1;
   static constexpr int kSmemBytes = kBarOffset + kNumBars * 8 + 16 + 1024;  // + align slack
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
 __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int group_m, int& tm, int& tn) {
@@ -100,12 +107,67 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
   tn = r / gm;
 }
 
+// Epilogue of one warp for one accumulator tile: 32 TMEM lanes (= 32 output rows) x NCOLS
+// FP32 columns. Each chunk (128 B per row: 32 fp32 or 64 bf16) goes registers -> one of the
+// warp's two 4 KB staging buffers in shared memory, 128B-swizzled like the C tensor map so
+// the 16-byte writes of a warp spread over all banks, and leaves through one TMA store
+// (full 128 B lines; rows/columns outside C are clipped by the TMA unit). `release` runs
+// once the last TMEM load of the tile has completed, so the MMA warp can reuse the buffer.
+
+template <Out OUT, int NCOLS, typename Release>
+__device__ __forceinline__ void epilogue_tile(uint32_t tbase, const CUtensorMap* tmC, int x0, int y0, float alpha,
+                                              uint8_t* wbuf, int& uses, int lane, Release release) {
+  constexpr int kCols = (OUT == Out::F32) ? 32 : 64;  // columns per 128-byte row chunk
+  const uint32_t row_addr = smem_u32(wbuf) + lane * 128;
+#pragma unroll 1
+  for (int c = 0; c < NCOLS; c += kCols) {
+    uint32_t r[kCols];
+    tmem_ld_32x32b_x32(tbase + c, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+    if constexpr (kCols == 64) tmem_ld_32x32b_x32(tbase + c + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+    tmem_ld_wait();
+    if (c + kCols >= NCOLS) release();
+    const int bsel = uses & 1;
+    if (uses >= 2) {
+      if (lane == 0) bulk_wait_group_read<1>();
+      __syncwarp();
+    }
+    const uint32_t base = row_addr + bsel * kEpiBufBytes;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t dst = base + ((j ^ (lane & 7)) << 4);
+      if constexpr (OUT == Out::F32) {
+        st_shared_v4(dst, __float_as_uint(__uint_as_float(r[4 * j]) * alpha),
+                     __float_as_uint(__uint_as_float(r[4 * j + 1]) * alpha),
+                     __float_as_uint(__uint_as_float(r[4 * j + 2]) * alpha),
+                     __float_as_uint(__uint_as_float(r[4 * j + 3]) * alpha));
+      } else {
+        uint32_t w[4];
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          __nv_bfloat162 v = __floats2bfloat162_rn(__uint_as_float(r[8 * j + 2 * h]) * alpha,
+                                                   __uint_as_float(r[8 * j + 2 * h + 1]) * alpha);
+          w[h] = *reinterpret_cast<uint32_t*>(&v);
+        }
+        st_shared_v4(dst, w[0], w[1], w[2], w[3]);
+      }
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(tmC, wbuf + bsel * kEpiBufBytes, x0 + c, y0);
+      bulk_commit_group();
+    }
+    ++uses;
+  }
+}
+
 template <Kind KIND, bool B_MN, int BN, int STAGES, int ACC_BUFS, Out OUT>
 __global__ void __launch_bounds__(kThreads, 1)
     bw_tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                      const GemmParams p) {
+                      const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
   using Cfg = GemmCfg<KIND, B_MN, BN, STAGES, ACC_BUFS>;
   constexpr int KE = KindTraits<KIND>::kElemsPerSlab;
+  constexpr int KX = KindTraits<KIND>::kCoordPerSlab;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kBarOffset);
@@ -141,7 +203,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 0 && lane == 0) { tma_prefetch_desc(&tmA); tma_prefetch_desc(&tmB); }
+  if (warp == 0 && lane == 0) { tma_prefetch_desc(&tmA); tma_prefetch_desc(&tmB); tma_prefetch_desc(&tmC); }
   if (warp == 1) { tmem_alloc(tmem_slot, Cfg::kTmemCols); tmem_relinquish(); }
   tc_fence_before();
   __syncthreads();
@@ -174,13 +236,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             tx += sfa_bytes * (1 + sfb_rbs);
           }
           mbar_arrive_expect_tx(&full[s], tx);
-          tma_load_2d(&tmA, &full[s], sA, kb * KE, tm * kBM, pol_a);
+          tma_load_2d(&tmA, &full[s], sA, kb * KX, tm * kBM, pol_a);
           if constexpr (B_MN) {
 #pragma unroll
             for (int j = 0; j < BN / 64; ++j)
               tma_load_2d(&tmB, &full[s], sB + j * 64 * kSlabBytes, tn * BN + 64 * j, kb * 64, pol_b);
           } else {
-            tma_load_2d(&tmB, &full[s], sB, kb * KE, tn * BN, pol_b);
+            tma_load_2d(&tmB, &full[s], sB, kb * KX, tn * BN, pol_b);
           }
           if (KIND == Kind::MXF4 && p.sfa != nullptr) {
             // Scale factors: tiled layout = [row block][k group of 4 SF][512 B]. One stage
@@ -267,7 +329,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
     const int q = warp & 3;                  // TMEM lane quarter this warp may access
-    const int row_in_tile = q * 32 + lane;
+    uint8_t* wbuf = smem + Cfg::kEpiOffset + (warp - 2) * 2 * kEpiBufBytes;
+    int uses = 0;
     float alpha = 1.f;
     if (p.scale_a) alpha *= __ldg(p.scale_a);
     if (p.scale_b) alpha *= __ldg(p.scale_b);
@@ -279,54 +342,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t aph = (local / ACC_BUFS) & 1;
       if (!mbar_wait(&accfull[b], aph, wc, 5)) break;
       tc_fence_after();
-      const int row = tm * kBM + row_in_tile;
-      const int col0 = tn * BN;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * BN;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tbase + c * 32, r);
-        tmem_ld_wait();
-        if (c == BN / 32 - 1) { tc_fence_before(); mbar_arrive(&accempty[b]); }
-        const int col = col0 + c * 32;
-        if (row < p.M) {
-          if constexpr (OUT == Out::F32) {
-            float* dst = reinterpret_cast<float*>(p.C) + static_cast<size_t>(row) * p.ldc + col;
-            if (col + 32 <= p.N) {
-#pragma unroll
-              for (int j = 0; j < 32; j += 4) {
-                float4 v = make_float4(__uint_as_float(r[j]) * alpha, __uint_as_float(r[j + 1]) * alpha,
-                                       __uint_as_float(r[j + 2]) * alpha, __uint_as_float(r[j + 3]) * alpha);
-                *reinterpret_cast<float4*>(dst + j) = v;
-              }
-            } else {
-              for (int j = 0; j < 32; ++j)
-                if (col + j < p.N) dst[j] = __uint_as_float(r[j]) * alpha;
-            }
-          } else {
-            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.C) + static_cast<size_t>(row) * p.ldc + col;
-            if (col + 32 <= p.N) {
-#pragma unroll
-              for (int j = 0; j < 32; j += 8) {
-                uint4 v;
-                __nv_bfloat162 h0 = __floats2bfloat162_rn(__uint_as_float(r[j]) * alpha, __uint_as_float(r[j + 1]) * alpha);
-                __nv_bfloat162 h1 = __floats2bfloat162_rn(__uint_as_float(r[j + 2]) * alpha, __uint_as_float(r[j + 3]) * alpha);
-                __nv_bfloat162 h2 = __floats2bfloat162_rn(__uint_as_float(r[j + 4]) * alpha, __uint_as_float(r[j + 5]) * alpha);
-                __nv_bfloat162 h3 = __floats2bfloat162_rn(__uint_as_float(r[j + 6]) * alpha, __uint_as_float(r[j + 7]) * alpha);
-                v.x = *reinterpret_cast<uint32_t*>(&h0);
-                v.y = *reinterpret_cast<uint32_t*>(&h1);
-                v.z = *reinterpret_cast<uint32_t*>(&h2);
-                v.w = *reinterpret_cast<uint32_t*>(&h3);
-                *reinterpret_cast<uint4*>(dst + j) = v;
-              }
-            } else {
-              for (int j = 0; j < 32; ++j)
-                if (col + j < p.N) dst[j] = __float2bfloat16_rn(__uint_as_float(r[j]) * alpha);
-            }
-          }
-        }
-      }
+      epilogue_tile<OUT, BN>(tbase, &tmC, tn * BN, tm * kBM + q * 32, alpha, wbuf, uses, lane, [&] {
+        tc_fence_before();
+        mbar_arrive(&accempty[b]);
+      });
     }
+    if (lane == 0) bulk_wait_group<0>();
   }
 
   tc_fence_before();

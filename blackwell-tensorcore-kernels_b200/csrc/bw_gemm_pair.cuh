@@ -1,0 +1,192 @@
+// CTA-pair (cta_group::2) variant of the persistent tcgen05 GEMM: 256 x 256 output tiles.
+//
+// A cluster of two CTAs on neighbouring SMs shares one 256 x 256 accumulator tile: CTA r
+// loads rows [128r, 128r+128) of A and columns [128r, 128r+128) of B for every k-slab into
+// its own shared memory (no multicast; each TMA load targets its own CTA), and the leader
+// CTA's single MMA thread issues tcgen05.mma.cta_group::2 with M = 256, N = 256, which reads
+// both CTAs' slabs and accumulates rows [128r, 128r+128) in CTA r's Tensor Memory. Per CTA
+// and k-slab this moves 32 KB instead of the 48 KB of a 128 x 256 single-CTA tile for the
+// same MMA work, which is what keeps the L2 -> SM feed below the tensor-core rate.
+//
+// Synchronisation:
+//   full[s]    (leader)  producer of the leader expects both CTAs' bytes; both CTAs' TMA
+//                        loads complete on it.
+//   empty[s]   (each)    the leader's MMA thread commits to its own and to the peer's copy.
+//   accfull[b] (each)    accumulator b ready: committed to both CTAs.
+//   accempty[b](leader)  4 epilogue warps of each CTA arrive (8 arrivals).
+// Every wait is bounded; all CTAs reach the closing cluster barrier on every path.
+#pragma once
+#include "bw_gemm_kernel.cuh"
+
+namespace bw {
+
+template <Kind KIND, int STAGES>
+struct PairCfg {
+  static constexpr int kABytes = 128 * kSlabBytes;  // this CTA's 128 rows of A
+  static constexpr int kBBytes = 128 * kSlabBytes;  // this CTA's 128 columns of B
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kEpiOffset = STAGES * kStageBytes;
+  static constexpr int kBarOffset = kEpiOffset + kEpiBytes;
+  static constexpr int kNumBars = 2 * STAGES + 2 * 2 + 1;
+  static constexpr int kSmemBytes = kBarOffset + kNumBars * 8 + 16 + 1024;
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
+  static constexpr int kTmemCols = 512;  // two 256-column FP32 accumulators
+};
+
+template <Kind KIND, bool B_MN, int STAGES, Out OUT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    bw_tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                           const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
+  using Cfg = PairCfg<KIND, STAGES>;
+  constexpr int KX = KindTraits<KIND>::kCoordPerSlab;
+  constexpr int KE = KindTraits<KIND>::kElemsPerSlab;
+  constexpr int TM = 256, TN = 256;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kBarOffset);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* accfull = bars + 2 * STAGES;
+  uint64_t* accempty = bars + 2 * STAGES + 2;
+  uint64_t* teardown = bars + 2 * STAGES + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::kNumBars);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const uint32_t peer = rank ^ 1u;
+  const bool leader = rank == 0;
+  const int cluster = blockIdx.x >> 1;
+  const int nclusters = gridDim.x >> 1;
+  const int tiles_m = (p.M + TM - 1) / TM;
+  const int tiles_n = (p.N + TN - 1) / TN;
+  const int num_tiles = tiles_m * tiles_n;
+  const int nk = (p.K + KE - 1) / KE;
+  const WaitCtl wc{abort_flag, p.status, p.budget_ns};
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    for (int b = 0; b < 2; ++b) { mbar_init(&accfull[b], 1); mbar_init(&accempty[b], 2 * kEpiWarps); }
+    mbar_init(teardown, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) { tma_prefetch_desc(&tmA); tma_prefetch_desc(&tmB); tma_prefetch_desc(&tmC); }
+  if (warp == 1) { tmem_alloc_pair(tmem_slot, Cfg::kTmemCols); tmem_relinquish_pair(); }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer (both CTAs) ----------------
+    if (lane == 0) {
+      const uint64_t pol = l2_policy_evict_last();
+      const uint32_t full_leader = mapa_shared(smem_u32(full), 0);
+      int s = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int t = cluster; t < num_tiles && ok; t += nclusters) {
+        int tm, tn;
+        tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
+        const int arow = tm * TM + static_cast<int>(rank) * 128;
+        const int bcol = tn * TN + static_cast<int>(rank) * 128;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&empty[s], ph ^ 1, wc, 11)) { ok = false; break; }
+          uint8_t* sA = smem + s * Cfg::kStageBytes;
+          uint8_t* sB = sA + Cfg::kABytes;
+          if (leader) mbar_arrive_expect_tx(&full[s], 2 * Cfg::kStageBytes);
+          const uint32_t fb = full_leader + s * 8;
+          tma_load_2d_pair(&tmA, fb, sA, kb * KX, arow, pol);
+          if constexpr (B_MN) {
+            tma_load_2d_pair(&tmB, fb, sB, bcol, kb * 64, pol);
+            tma_load_2d_pair(&tmB, fb, sB + 64 * kSlabBytes, bcol + 64, kb * 64, pol);
+          } else {
+            tma_load_2d_pair(&tmB, fb, sB, kb * KX, bcol, pol);
+          }
+          if (++s == STAGES) { s = 0; ph ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (leader CTA only) ----------------
+    if (leader && lane == 0) {
+      const uint32_t idesc = idesc_dense(KindTraits<KIND>::kFmt, KindTraits<KIND>::kFmt, B_MN, 256, 256);
+      const uint32_t empty_own = smem_u32(empty), empty_peer = mapa_shared(smem_u32(empty), peer);
+      const uint32_t accfull_own = smem_u32(accfull), accfull_peer = mapa_shared(smem_u32(accfull), peer);
+      int s = 0;
+      uint32_t ph = 0;
+      int local = 0;
+      bool ok = true;
+      for (int t = cluster; t < num_tiles && ok; t += nclusters, ++local) {
+        const int b = local & 1;
+        const uint32_t aph = (local >> 1) & 1;
+        if (!mbar_wait(&accempty[b], aph ^ 1, wc, 12)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + b * 256;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&full[s], ph, wc, 13)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t aaddr = smem_u32(smem + s * Cfg::kStageBytes);
+          const uint32_t baddr = aaddr + Cfg::kABytes;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
+            const uint64_t adesc = sdesc_sw128(aaddr + k * 32, 16, 1024);
+            uint64_t bdesc;
+            if constexpr (B_MN) bdesc = sdesc_sw128(baddr + k * 16 * kSlabBytes, 64 * kSlabBytes, 1024);
+            else bdesc = sdesc_sw128(baddr + k * 32, 16, 1024);
+            if constexpr (KIND == Kind::F16) umma_f16_pair(d_tmem, adesc, bdesc, idesc, acc);
+            else umma_f8f6f4_pair(d_tmem, adesc, bdesc, idesc, acc);
+          }
+          umma_commit_pair(empty_own + s * 8);
+          umma_commit_pair(empty_peer + s * 8);
+          if (++s == STAGES) { s = 0; ph ^= 1; }
+        }
+        if (ok) {
+          umma_commit_pair(accfull_own + b * 8);
+          umma_commit_pair(accfull_peer + b * 8);
+        }
+      }
+      umma_commit_pair(smem_u32(teardown));
+      mbar_wait(teardown, 0, wc, 14);
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
+    const int q = warp & 3;
+    uint8_t* wbuf = smem + Cfg::kEpiOffset + (warp - 2) * 2 * kEpiBufBytes;
+    int uses = 0;
+    const uint32_t accempty_leader = mapa_shared(smem_u32(accempty), 0);
+    float alpha = 1.f;
+    if (p.scale_a) alpha *= __ldg(p.scale_a);
+    if (p.scale_b) alpha *= __ldg(p.scale_b);
+    int local = 0;
+    for (int t = cluster; t < num_tiles; t += nclusters, ++local) {
+      int tm, tn;
+      tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
+      const int b = local & 1;
+      const uint32_t aph = (local >> 1) & 1;
+      if (!mbar_wait(&accfull[b], aph, wc, 15)) break;
+      tc_fence_after();
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * 256;
+      epilogue_tile<OUT, TN>(tbase, &tmC, tn * TN, tm * TM + static_cast<int>(rank) * 128 + q * 32, alpha, wbuf,
+                             uses, lane, [&] {
+                               tc_fence_before();
+                               __syncwarp();
+                               if (lane == 0) mbar_arrive_cluster(accempty_leader + b * 8);
+                             });
+    }
+    if (lane == 0) bulk_wait_group<0>();
+  }
+
+  tc_fence_before();
+  cluster_sync();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+}  // namespace bw
