@@ -1,0 +1,499 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 tensor-core GEMM library (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload f16|fp8|mxfp4|fp4] [--gather] [--no-compare]
+
+A step is one GEMM over one batch of synthetic inputs already resident in HBM:
+  N = 1: C = A x B at M = N = K = 8192 (FP16 in, FP32 accumulate,
+         FP32 out, uniform[-1, 1] seeded inputs rounded to FP16).
+  N > 1: one process per GPU; rank r computes the column shard C[:, r*8192:(r+1)*8192] =
+         A x B[:, shard r] of an 8192 x (8192 N) x 8192 GEMM (weak scaling; no collective in
+         the timed region; --gather adds an NCCL all-gather of C afterwards, untimed).
+`value` is whole-job TFLOP/s = (all ranks' FLOPs) / (max over ranks of the device time of
+K steps). `e2e` is the same GEMM through the public C ABI with the inputs coming from pinned
+host memory and C going back to the host inside the timed region. A (128 MiB) + B (128 MiB)
+exceed the 126 MB L2, so no flush is needed between steps.
+
+--impl reference runs the reference's own stock launcher for the same workload
+(launch_mma_warptile, the reference's headline FP16 kernel, built from its sources for
+sm_100a by oracle/build_ref.sh) through its launch_* API; its CPU-oracle baseline is
+reported in `cpu_baseline` of our line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(REPO, "blackwell-tensorcore-kernels_b200")
+ORACLE = os.path.join(REPO, "oracle")
+for _p in (PKG, ORACLE):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+DIM = 8192
+
+
+def load_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return d, "measured"
+    except (OSError, ValueError):
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+def profile_traffic(name: str):
+    """DRAM bytes per launch recorded from an ncu capture in profiles/<name>.md
+    (line `traffic_bytes_per_launch: <int>`), or None."""
+    path = os.path.join(REPO, "profiles", name + ".md")
+    try:
+        for line in open(path):
+            if line.strip().startswith("traffic_bytes_per_launch:"):
+                return int(float(line.split(":", 1)[1]))
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """SM clock and clock-event (throttle) reasons polled through NVML every 10 ms from
+    start() to stop(), i.e. across the timed region."""
+
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4}
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.samples: list[tuple[float, int]] = []
+        self.smax = 0.0
+        self._stop = threading.Event()
+        self.t = None
+        self.ok = False
+
+    def start(self):
+        try:
+            import pynvml as nv
+
+            nv.nvmlInit()
+            h = nv.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.smax = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+        except Exception:
+            return
+        self.ok = True
+
+        def poll():
+            while not self._stop.is_set():
+                try:
+                    clk = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                    rs = int(nv.nvmlDeviceGetCurrentClocksEventReasons(h))
+                    self.samples.append((clk, rs))
+                except Exception:
+                    pass
+                self._stop.wait(0.01)
+
+        self.t = threading.Thread(target=poll, daemon=True)
+        self.t.start()
+
+    def mark(self):
+        """Index of the next sample (to select the samples of a sub-interval)."""
+        return len(self.samples)
+
+    def stop(self, since: int = 0):
+        if not self.ok:
+            return None
+        self._stop.set()
+        self.t.join(timeout=2)
+        sm = [c for c, _ in self.samples[since:]]
+        if not sm:
+            sm = [c for c, _ in self.samples]
+        reasons = sorted({n for _, r in self.samples[since:] for n, bit in self.REASONS.items() if r & bit})
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": self.smax, "reasons": reasons,
+                "samples": len(self.samples) - since, "source": "NVML, 10 ms polling during the timed region"}
+
+
+def dist_setup(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def timed_steps(step, K: int, W: int, world: int, stream):
+    """W warm-up steps, then K steps bracketed by barrier + synchronize; returns device ms
+    per step (CUDA events on the launching stream), max over ranks."""
+    import torch
+
+    for _ in range(W):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    s = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for _ in range(K):
+        step()
+    e.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = s.elapsed_time(e) / K
+    return max_over_ranks(ms, world)
+
+
+def make_inputs(workload: str, rank: int, dev):
+    """Seeded synthetic inputs of the BASELINE shapes (per rank: its own column shard)."""
+    import torch
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + 17 * rank)
+    M = N = K = DIM
+    if workload == "f16":
+        A = (torch.rand((M, K), generator=g, device=dev) * 2 - 1).half()
+        B = (torch.rand((K, N), generator=g, device=dev) * 2 - 1).half()
+        return {"A": A, "B": B}
+    A32 = torch.randn((M, K), generator=g, device=dev)
+    B32 = torch.randn((K, N), generator=g, device=dev)
+    return {"A32": A32, "B32": B32}
+
+
+def cpu_baseline(threads: int, budget_s: float = 12.0):
+    """FP64 oracle GEMM (oracle/bw_oracle.c) on host cores over a bounded row sample of the
+    8192^3 FP16 workload; returns TFLOP/s and the sample description."""
+    import numpy as np
+
+    import oracle as o
+
+    K = N = DIM
+    rng = np.random.default_rng(5)
+    B = o.f16_to_f32(o.f32_to_f16(rng.uniform(-1, 1, size=(K, N)).astype(np.float32)))
+    # double the row sample until one run takes at least budget_s / 2 (capped at all rows)
+    rows = 64
+    while True:
+        A = o.f16_to_f32(o.f32_to_f16(rng.uniform(-1, 1, size=(rows, K)).astype(np.float32)))
+        t0 = time.perf_counter()
+        o.gemm_f64(A, B, threads=threads)
+        dt = time.perf_counter() - t0
+        if dt >= budget_s / 2 or rows >= DIM:
+            break
+        rows = min(DIM, rows * max(2, int(budget_s / 2 / max(dt, 1e-3))))
+    flops = 2.0 * rows * N * K
+    return flops / dt / 1e12, f"{rows} x {N} x {K} rows of the 8192^3 fp16 GEMM, FP64 oracle, {dt:.1f} s"
+
+
+# ---------------------------------------------------------------------------------------
+def run_ours(args, world, rank, local):
+    import numpy as np
+    import torch
+
+    import bwgemm
+
+    dev = torch.device("cuda", local)
+    bwgemm.init(local)
+    stream = torch.cuda.current_stream()
+    M = N = K = DIM
+    flops = 2.0 * M * N * K
+    clocks = ClockSampler(local)
+    clocks.start()
+    inp = make_inputs(args.workload, rank, dev)
+    wl = args.workload
+    if wl == "f16":
+        A, B = inp["A"], inp["B"]
+        C = torch.empty((M, N), dtype=torch.float32, device=dev)
+        step = lambda: bwgemm.gemm_f16(A, B, C, stream=stream)  # noqa: E731
+        dtype, in_bytes, out_bytes = "f16", 2, 4
+    elif wl == "fp8":
+        qa, sa = bwgemm.quantize_fp8(inp["A32"], False, bwgemm.SCALE_AMAX)
+        qb, sb = bwgemm.quantize_fp8(inp["B32"], True, bwgemm.SCALE_AMAX)
+        C = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+        step = lambda: bwgemm.gemm_fp8(qa, qb, sa, sb, C, stream=stream)  # noqa: E731
+        dtype, in_bytes, out_bytes = "e4m3", 1, 2
+    elif wl in ("mxfp4", "fp4"):
+        if wl == "mxfp4":
+            qa, sfa = bwgemm.quantize_mxfp4(inp["A32"], False, bwgemm.MX_BLOCK32)
+            qb, sfb = bwgemm.quantize_mxfp4(inp["B32"], True, bwgemm.MX_BLOCK32)
+            C = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+            step = lambda: bwgemm.gemm_mxfp4(qa, qb, sfa, sfb, K, C=C, stream=stream)  # noqa: E731
+        else:
+            qa, sa = bwgemm.quantize_fp4(inp["A32"], False, bwgemm.SCALE_AMAX, bwgemm.FP4_PACKED)
+            qb, sb = bwgemm.quantize_fp4(inp["B32"], True, bwgemm.SCALE_AMAX, bwgemm.FP4_PACKED)
+            C = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+            step = lambda: bwgemm.gemm_fp4(qa, qb, K, sa, sb, C=C, stream=stream)  # noqa: E731
+        dtype, in_bytes, out_bytes = "e2m1", 0.5, 2
+    else:
+        raise SystemExit(f"unknown workload {wl}")
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    mark = clocks.mark()
+    ms = timed_steps(step, args.steps, 0, world, stream)
+    clk = clocks.stop(mark)
+    status = bwgemm.device_status()
+    if status != 0:
+        raise SystemExit(f"kernel reported status {status}")
+    value = world * flops / (ms * 1e-3) / 1e12
+
+    # ---- e2e: pinned host inputs -> device, GEMM through the C ABI, C -> pinned host
+    e2e = None
+    if wl == "f16":
+        hA = torch.empty((M, K), dtype=torch.float16, pin_memory=True)
+        hB = torch.empty((K, N), dtype=torch.float16, pin_memory=True)
+        hA.copy_(A.cpu())
+        hB.copy_(B.cpu())
+        hC = torch.empty((M, N), dtype=torch.float32, pin_memory=True)
+        dA = torch.empty_like(A)
+        dB = torch.empty_like(B)
+
+        def e2e_step():
+            dA.copy_(hA, non_blocking=True)
+            dB.copy_(hB, non_blocking=True)
+            bwgemm.gemm_f16(dA, dB, C, stream=stream)
+            hC.copy_(C, non_blocking=True)
+
+        e_steps = max(3, min(args.steps, 10))
+        ems = timed_steps(e2e_step, e_steps, 2, world, stream)
+        e2e = {"value": round(world * flops / (ems * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+               "h2d_bytes_per_step": int(hA.numel() * 2 + hB.numel() * 2), "d2h_bytes_per_step": int(hC.numel() * 4),
+               "ms_per_step": round(ems, 4)}
+        # the result that came back must be the product (spot-check 4 rows on the host)
+        rows = [0, 1, M // 2, M - 1]
+        ref = (hA[rows].float() @ hB.float())
+        assert torch.allclose(hC[rows], ref, atol=2 ** -10 * (K ** 0.5), rtol=0), "e2e result mismatch"
+
+    peaks, peak_src = load_peaks()
+    if wl == "f16":
+        peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+        peak_name = "bf16_tflops (burst, cuBLAS bf16 8192^3)"
+    else:
+        # no measured FP8/FP4 library peak in MEASURED_PEAKS.json: scale the measured bf16
+        # figure by the nominal dense-rate ratio (2x FP8, 4x FP4)
+        mult = 2.0 if wl == "fp8" else 4.0
+        peak = mult * float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+        peak_name = f"{mult:.0f} x bf16_tflops (burst)"
+    achieved = flops / (ms * 1e-3) / 1e12
+    traffic = profile_traffic({"f16": "bw_tc_gemm_pair_f16_8192", "fp8": "bw_tc_gemm_pair_fp8_8192",
+                               "mxfp4": "bw_tc_gemm_mxfp4_8192", "fp4": "bw_tc_gemm_mxfp4_8192"}[wl])
+    roofline = {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(peak, 1), "unit": "TFLOP/s",
+                "frac": round(achieved / peak, 4), "traffic": traffic,
+                "peak_source": f"{peak_src}: {peak_name}",
+                "algorithmic_flops_per_launch": flops}
+
+    comparisons = {}
+    if not args.no_compare and rank == 0 and world == 1:
+        comparisons = compare_rows(args, wl, inp, dev, stream)
+
+    line = {
+        "metric": "TFLOP/s & % of B200 dense peak (FP16/FP8/MXFP4 8192^3); box TFLOP/s @1/2/4/8",
+        "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": dtype, "data": "synthetic (seeded uniform[-1,1] rounded to FP16)" if wl == "f16"
+        else "synthetic (seeded N(0,1), quantised on device)",
+        "config": {"workload": f"{wl}_gemm_8192x8192x8192_per_gpu", "M": M, "N_per_gpu": N, "K": K,
+                   "N_total": N * world, "parallelism": f"column shards x{world} (no collective in the timed region)",
+                   "l2": "inputs larger than L2 (A and B 8192x8192 each)",
+                   "accumulate": "fp32", "out": "fp32" if wl == "f16" else "bf16"},
+        "e2e": e2e,
+        "roofline": roofline,
+        "gpu_launches": args.steps,
+        "clocks": clk,
+        "impl": "ours",
+    }
+    if comparisons:
+        line["comparisons"] = comparisons
+    if rank == 0 and world == 1 and not args.no_cpu:
+        threads = os.cpu_count() or 1
+        v, sample = cpu_baseline(threads)
+        line["cpu_baseline"] = {"value": round(v, 5), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                                "sample": sample}
+    return line
+
+
+def compare_rows(args, wl, inp, dev, stream):
+    """Library rows measured in the same run (cuBLAS / cuBLASLt through torch) and our other
+    precisions; each timed like the headline (warm-up, CUDA events, 20 launches)."""
+    import torch
+
+    import bwgemm
+
+    M = N = K = DIM
+    flops = 2.0 * M * N * K
+    out = {}
+
+    def tf(fn, n=20):
+        ms = timed_steps(fn, n, 3, 1, stream)
+        return round(flops / (ms * 1e-3) / 1e12, 1)
+
+    try:
+        if wl == "f16":
+            A, B = inp["A"], inp["B"]
+            out["cublas_f16_f32out_tflops"] = tf(lambda: torch.mm(A, B, out_dtype=torch.float32))
+            out["cublas_f16_f16out_tflops"] = tf(lambda: torch.mm(A, B))
+            A32 = (A.float() * 2)
+            B32 = (B.float() * 2)
+            qa, sa = bwgemm.quantize_fp8(A32, False, bwgemm.SCALE_AMAX)
+            qb, sb = bwgemm.quantize_fp8(B32, True, bwgemm.SCALE_AMAX)
+            C8 = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+            out["ours_fp8_bf16out_tflops"] = tf(lambda: bwgemm.gemm_fp8(qa, qb, sa, sb, C8, stream=stream))
+            a8 = qa.view(torch.float8_e4m3fn)
+            b8 = qb.view(torch.float8_e4m3fn).t()
+            out["cublaslt_fp8_bf16out_tflops"] = tf(
+                lambda: torch._scaled_mm(a8, b8, scale_a=sa, scale_b=sb, out_dtype=torch.bfloat16))
+            q4a, sfa = bwgemm.quantize_mxfp4(A32, False, bwgemm.MX_BLOCK32)
+            q4b, sfb = bwgemm.quantize_mxfp4(B32, True, bwgemm.MX_BLOCK32)
+            out["ours_mxfp4_bf16out_tflops"] = tf(lambda: bwgemm.gemm_mxfp4(q4a, q4b, sfa, sfb, K, C=C8, stream=stream))
+    except Exception as ex:  # a missing library path must not hide the headline number
+        out["error"] = f"{type(ex).__name__}: {ex}"[:200]
+    return out
+
+
+# ---------------------------------------------------------------------------------------
+def run_reference(args, world, rank, local):
+    """The reference's stock FP16 launcher (launch_mma_warptile) on the same workload."""
+    import ctypes
+
+    import torch
+
+    lib_path = os.path.join(ORACLE, "_ref", "libref_kernels.so")
+    base = {"impl": "reference", "metric": "TFLOP/s & % of B200 dense peak (FP16/FP8/MXFP4 8192^3); box TFLOP/s @1/2/4/8"}
+    if not os.path.exists(lib_path):
+        base["unavailable"] = "oracle/_ref/libref_kernels.so was not built (oracle/build_ref.sh needs the reference sources)"
+        return base
+    L = ctypes.CDLL(lib_path)
+    L.ref_launch.argtypes = [ctypes.c_char_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
+                             ctypes.c_int, ctypes.c_int]
+    L.ref_launch.restype = ctypes.c_int
+    dev = torch.device("cuda", local)
+    # The reference's launchers run on the legacy default stream (src/main.cu:91-92).
+    stream = torch.cuda.default_stream(dev)
+    M = N = K = DIM
+    flops = 2.0 * M * N * K
+    name = b"mma_warptile"
+    inp = make_inputs("f16", rank, dev)
+    A = inp["A"].float().contiguous()
+    B = inp["B"].float().contiguous()
+    C = torch.empty((M, N), dtype=torch.float32, device=dev)
+
+    def step():
+        rc = L.ref_launch(name, A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K)
+        if rc != 0:
+            raise RuntimeError(f"reference launch failed: {rc}")
+
+    with torch.cuda.stream(stream):
+        clocks = ClockSampler(local)
+        clocks.start()
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        mark = clocks.mark()
+        ms = timed_steps(step, args.steps, 0, world, stream)
+        clk = clocks.stop(mark)
+        value = world * flops / (ms * 1e-3) / 1e12
+        # e2e through the reference's API: FP32 host inputs -> device, launch (which stages
+        # FP16 on a new pointer), FP32 C -> host
+        hA = torch.empty((M, K), dtype=torch.float32, pin_memory=True)
+        hB = torch.empty((K, N), dtype=torch.float32, pin_memory=True)
+        hA.copy_(A.cpu())
+        hB.copy_(B.cpu())
+        hC = torch.empty((M, N), dtype=torch.float32, pin_memory=True)
+
+        def e2e_step():
+            A.copy_(hA, non_blocking=True)
+            B.copy_(hB, non_blocking=True)
+            step()
+            hC.copy_(C, non_blocking=True)
+
+        e_steps = max(3, min(args.steps, 10))
+        ems = timed_steps(e2e_step, e_steps, 2, world, stream)
+    e2e_v = round(world * flops / (ems * 1e-3) / 1e12, 2)
+    line = dict(base)
+    line.update({
+        "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f16", "data": "synthetic (seeded uniform[-1,1]; the launcher casts to FP16 once per pointer)",
+        "config": {"workload": "f16_gemm_8192x8192x8192_per_gpu", "M": M, "N_per_gpu": N, "K": K,
+                   "N_total": N * world, "parallelism": f"column shards x{world}",
+                   "kernel": "reference launch_mma_warptile (mma.sync m16n8k16, built for sm_100a)"},
+        "e2e": {"value": e2e_v, "unit": "TFLOP/s", "h2d_bytes_per_step": int(hA.numel() * 4 + hB.numel() * 4),
+                "d2h_bytes_per_step": int(hC.numel() * 4)},
+        "clocks": clk,
+        "cpu_baseline": {"value": e2e_v, "unit": "TFLOP/s", "cores": 0, "kind": "reference",
+                         "sample": "the reference has no CPU GEMM; this arm runs its own GPU launcher "
+                                   "(launch_mma_warptile) on the full workload"},
+    })
+    return line
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["f16", "fp8", "mxfp4", "fp4"], default="f16")
+    ap.add_argument("--gather", action="store_true", help="all-gather C over NCCL after timing (untimed)")
+    ap.add_argument("--no-compare", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        # reference arm: under torchrun rank 0 alone runs it; the other ranks exit without work
+        if int(os.environ.get("RANK", "0")) != 0:
+            return
+        import torch
+
+        local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(local)
+        line = run_reference(args, 1, 0, local)
+        print(json.dumps(line), flush=True)
+        return
+    world, rank, local = dist_setup(args)
+    line = run_ours(args, world, rank, local)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

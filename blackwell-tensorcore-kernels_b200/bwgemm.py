@@ -66,6 +66,7 @@ def lib():
         "bw_num_sms": [I],
         "bw_device_status": [P, P],
         "bw_set_wait_budget_ns": [ctypes.c_ulonglong],
+        "bw_set_trace_buffer": [P, I],
         "bw_gemm_f16": [P, P, P, I, I, I, P],
         "bw_gemm_f16_bt": [P, P, P, I, I, I, P],
         "bw_gemm_fp8": [P, P, P, P, P, I, I, I, I, P],
@@ -127,6 +128,14 @@ def device_status(stream=None) -> int:
 
 def set_wait_budget_ns(ns: int) -> None:
     _check(lib().bw_set_wait_budget_ns(int(ns)))
+
+
+def set_trace_buffer(buf=None) -> None:
+    """Arm the per-CTA wait-time trace with a torch int64 CUDA tensor of shape (ctas, 8)."""
+    if buf is None:
+        _check(lib().bw_set_trace_buffer(None, 0))
+    else:
+        _check(lib().bw_set_trace_buffer(buf.data_ptr(), buf.shape[0]))
 
 
 def sf_bytes(outer: int, K: int) -> int:

@@ -31,16 +31,17 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, 
   int grid = tiles < d.sms ? tiles : d.sms;
   const int cap = env_int("BW_MAX_CTAS", 0);
   if (cap > 0 && grid > cap) grid = cap;
+  p.trace = nullptr;  // the single-CTA kernel has no trace points
   kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, tc, p);
   BW_CUDA(cudaGetLastError());
   return BW_OK;
 }
 
-template <Kind KIND, bool B_MN, int STAGES, Out OUT>
+template <Kind KIND, bool B_MN, int STAGES, Out OUT, bool DIRECT_EPI = false>
 int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, GemmParams p,
                 cudaStream_t stream, const DeviceState& d) {
-  using Cfg = PairCfg<KIND, STAGES>;
-  auto kern = bw_tc_gemm_pair_kernel<KIND, B_MN, STAGES, OUT>;
+  using Cfg = PairCfg<KIND, STAGES, DIRECT_EPI>;
+  auto kern = bw_tc_gemm_pair_kernel<KIND, B_MN, STAGES, OUT, DIRECT_EPI>;
   static bool attr_done[64] = {};
   int dev = 0;
   BW_CUDA(cudaGetDevice(&dev));
@@ -75,6 +76,7 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
   int clusters = tiles < resident ? tiles : resident;
   const int cap = env_int("BW_MAX_CTAS", 0);
   if (cap > 1 && clusters > cap / 2) clusters = cap / 2;
+  p.trace = trace_buffer(2 * clusters);
   kern<<<2 * clusters, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, tc, p);
   BW_CUDA(cudaGetLastError());
   return BW_OK;
@@ -104,6 +106,7 @@ GemmParams base_params(const DeviceState& d, void* C, int M, int N, int K) {
   p.K = K;
   p.ldc = N;
   p.group_m = env_int("BW_GROUP_M", 16);
+  p.hints = env_int("BW_L2_HINTS", 1);
   if (p.group_m < 1) p.group_m = 1;
   p.status = d.status;
   p.budget_ns = wait_budget_ns();
@@ -150,6 +153,8 @@ int gemm_f16_impl(const void* A, const void* B, float* C, int M, int N, int K, c
   GemmParams p = base_params(*d, C, M, N, K);
   if (pair) {
     const int st = env_int("BW_STAGES", 6);
+    const bool direct = env_int("BW_EPI_DIRECT", 0) != 0 && (reinterpret_cast<uintptr_t>(C) & 31u) == 0;
+    if (b_mn && direct) return launch_pair<Kind::F16, true, 7, Out::F32, true>(ta, tb, tc, p, s, *d);
     if (b_mn && st == 4) return launch_pair<Kind::F16, true, 4, Out::F32>(ta, tb, tc, p, s, *d);
     if (b_mn && st == 5) return launch_pair<Kind::F16, true, 5, Out::F32>(ta, tb, tc, p, s, *d);
     if (b_mn) return launch_pair<Kind::F16, true, 6, Out::F32>(ta, tb, tc, p, s, *d);

@@ -35,6 +35,11 @@ constexpr int kBM = 128;          // rows of A per tile (one TMEM lane per row)
 constexpr int kSlabBytes = 128;   // bytes of K per k-slab row (one 128B swizzle atom)
 constexpr int kThreads = 192;     // 6 warps
 constexpr int kEpiWarps = 4;
+// Trace words per CTA (clock64 cycles unless noted): 0 total kernel cycles, 1 MMA waits on
+// full slabs, 2 MMA waits on a free accumulator, 3 producer waits on empty slabs,
+// 4 epilogue (warp 2) waits on a ready accumulator, 5 epilogue (warp 2) busy cycles,
+// 6 tiles processed, 7 k-slabs issued by the MMA thread.
+constexpr int kTraceWords = 8;
 constexpr int kEpiBufBytes = 32 * 128;                   // per-warp staging buffer: 32 rows x 128 B
 constexpr int kEpiBytes = kEpiWarps * 2 * kEpiBufBytes;  // two buffers per epilogue warp: 32 KB
 
@@ -69,7 +74,9 @@ struct GemmParams {
   const uint8_t* sfb;          // MXF4: B scale factors
   int sf_kgroups;              // MXF4: number of 4-block K groups per 128-row block
   int group_m;                 // raster: tile rows per group
+  int hints;                   // bit 0: A/B loads evict_last (else evict_normal); bit 1: C stores evict_first
   int* status;                 // device status word
+  unsigned long long* trace;   // optional per-CTA wait-time trace (kTraceWords per CTA), or null
   unsigned long long budget_ns;
 };
 
@@ -114,9 +121,56 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
 // (full 128 B lines; rows/columns outside C are clipped by the TMA unit). `release` runs
 // once the last TMEM load of the tile has completed, so the MMA warp can reuse the buffer.
 
+// Shared-memory-free epilogue: each thread writes its own row straight from registers with
+// 256-bit stores, so every store fills whole 32-byte sectors. Needs 32-byte aligned C and
+// N % 8 == 0 (checked on the host); used where the staging buffers would cost a pipeline stage.
+template <Out OUT, int NCOLS, typename Release>
+__device__ __forceinline__ void epilogue_tile_direct(uint32_t tbase, const GemmParams& p, int row, int col0,
+                                                     float alpha, Release release) {
+#pragma unroll 1
+  for (int c = 0; c < NCOLS; c += 32) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(tbase + c, r);
+    tmem_ld_wait();
+    if (c + 32 >= NCOLS) release();
+    if (row >= p.M) continue;
+    const int col = col0 + c;
+    if constexpr (OUT == Out::F32) {
+      float* dst = reinterpret_cast<float*>(p.C) + static_cast<size_t>(row) * p.ldc + col;
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        if (col + 8 * g >= p.N) break;
+        uint32_t v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = __float_as_uint(__uint_as_float(r[8 * g + j]) * alpha);
+        st_global_v8(dst + 8 * g, v);
+      }
+    } else {
+      __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.C) + static_cast<size_t>(row) * p.ldc + col;
+#pragma unroll
+      for (int g = 0; g < 2; ++g) {
+        if (col + 16 * g >= p.N) break;
+        uint32_t v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(r[16 * g + 2 * j]) * alpha,
+                                                   __uint_as_float(r[16 * g + 2 * j + 1]) * alpha);
+          v[j] = *reinterpret_cast<uint32_t*>(&h);
+        }
+        if (col + 16 * g + 16 <= p.N) {
+          st_global_v8(dst + 16 * g, v);
+        } else {  // N % 16 == 8: the last group holds 8 valid columns
+          *reinterpret_cast<uint4*>(dst + 16 * g) = make_uint4(v[0], v[1], v[2], v[3]);
+        }
+      }
+    }
+  }
+}
+
 template <Out OUT, int NCOLS, typename Release>
 __device__ __forceinline__ void epilogue_tile(uint32_t tbase, const CUtensorMap* tmC, int x0, int y0, float alpha,
-                                              uint8_t* wbuf, int& uses, int lane, Release release) {
+                                              uint8_t* wbuf, int& uses, int lane, uint64_t store_policy,
+                                              bool hinted, Release release) {
   constexpr int kCols = (OUT == Out::F32) ? 32 : 64;  // columns per 128-byte row chunk
   const uint32_t row_addr = smem_u32(wbuf) + lane * 128;
 #pragma unroll 1
@@ -154,7 +208,8 @@ __device__ __forceinline__ void epilogue_tile(uint32_t tbase, const CUtensorMap*
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) {
-      tma_store_2d(tmC, wbuf + bsel * kEpiBufBytes, x0 + c, y0);
+      if (hinted) tma_store_2d_hint(tmC, wbuf + bsel * kEpiBufBytes, x0 + c, y0, store_policy);
+      else tma_store_2d(tmC, wbuf + bsel * kEpiBufBytes, x0 + c, y0);
       bulk_commit_group();
     }
     ++uses;
@@ -213,8 +268,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      const uint64_t pol_a = l2_policy_evict_last();
-      const uint64_t pol_b = l2_policy_evict_last();
+      const uint64_t pol_a = (p.hints & 1) ? l2_policy_evict_last() : l2_policy_evict_normal();
+      const uint64_t pol_b = pol_a;
       int s = 0;
       uint32_t ph = 0;
       bool ok = true;
@@ -329,6 +384,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
     const int q = warp & 3;                  // TMEM lane quarter this warp may access
+    const uint64_t store_pol = l2_policy_evict_first();
     uint8_t* wbuf = smem + Cfg::kEpiOffset + (warp - 2) * 2 * kEpiBufBytes;
     int uses = 0;
     float alpha = 1.f;
@@ -343,7 +399,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(&accfull[b], aph, wc, 5)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * BN;
-      epilogue_tile<OUT, BN>(tbase, &tmC, tn * BN, tm * kBM + q * 32, alpha, wbuf, uses, lane, [&] {
+      epilogue_tile<OUT, BN>(tbase, &tmC, tn * BN, tm * kBM + q * 32, alpha, wbuf, uses, lane, store_pol,
+                             (p.hints & 2) != 0, [&] {
         tc_fence_before();
         mbar_arrive(&accempty[b]);
       });

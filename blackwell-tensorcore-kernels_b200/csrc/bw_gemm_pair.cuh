@@ -20,24 +20,24 @@
 
 namespace bw {
 
-template <Kind KIND, int STAGES>
+template <Kind KIND, int STAGES, bool DIRECT_EPI = false>
 struct PairCfg {
   static constexpr int kABytes = 128 * kSlabBytes;  // this CTA's 128 rows of A
   static constexpr int kBBytes = 128 * kSlabBytes;  // this CTA's 128 columns of B
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kEpiOffset = STAGES * kStageBytes;
-  static constexpr int kBarOffset = kEpiOffset + kEpiBytes;
+  static constexpr int kBarOffset = kEpiOffset + (DIRECT_EPI ? 0 : kEpiBytes);
   static constexpr int kNumBars = 2 * STAGES + 2 * 2 + 1;
   static constexpr int kSmemBytes = kBarOffset + kNumBars * 8 + 16 + 1024;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
   static constexpr int kTmemCols = 512;  // two 256-column FP32 accumulators
 };
 
-template <Kind KIND, bool B_MN, int STAGES, Out OUT>
+template <Kind KIND, bool B_MN, int STAGES, Out OUT, bool DIRECT_EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     bw_tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                            const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
-  using Cfg = PairCfg<KIND, STAGES>;
+  using Cfg = PairCfg<KIND, STAGES, DIRECT_EPI>;
   constexpr int KX = KindTraits<KIND>::kCoordPerSlab;
   constexpr int KE = KindTraits<KIND>::kElemsPerSlab;
   constexpr int TM = 256, TN = 256;
@@ -64,6 +64,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int num_tiles = tiles_m * tiles_n;
   const int nk = (p.K + KE - 1) / KE;
   const WaitCtl wc{abort_flag, p.status, p.budget_ns};
+  const bool tracing = p.trace != nullptr;
+  const long long t_start = clock64();
+  unsigned long long tr_a = 0, tr_b = 0, tr_c = 0;  // role-specific wait counters
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
@@ -82,7 +85,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ---------------- TMA producer (both CTAs) ----------------
     if (lane == 0) {
-      const uint64_t pol = l2_policy_evict_last();
+      const uint64_t pol = (p.hints & 1) ? l2_policy_evict_last() : l2_policy_evict_normal();
       const uint32_t full_leader = mapa_shared(smem_u32(full), 0);
       int s = 0;
       uint32_t ph = 0;
@@ -93,7 +96,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const int arow = tm * TM + static_cast<int>(rank) * 128;
         const int bcol = tn * TN + static_cast<int>(rank) * 128;
         for (int kb = 0; kb < nk; ++kb) {
+          const long long w0 = tracing ? clock64() : 0;
           if (!mbar_wait(&empty[s], ph ^ 1, wc, 11)) { ok = false; break; }
+          if (tracing) tr_a += clock64() - w0;
           uint8_t* sA = smem + s * Cfg::kStageBytes;
           uint8_t* sB = sA + Cfg::kABytes;
           if (leader) mbar_arrive_expect_tx(&full[s], 2 * Cfg::kStageBytes);
@@ -122,11 +127,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       for (int t = cluster; t < num_tiles && ok; t += nclusters, ++local) {
         const int b = local & 1;
         const uint32_t aph = (local >> 1) & 1;
+        const long long w1 = tracing ? clock64() : 0;
         if (!mbar_wait(&accempty[b], aph ^ 1, wc, 12)) { ok = false; break; }
+        if (tracing) tr_b += clock64() - w1;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + b * 256;
         for (int kb = 0; kb < nk; ++kb) {
+          const long long w2 = tracing ? clock64() : 0;
           if (!mbar_wait(&full[s], ph, wc, 13)) { ok = false; break; }
+          if (tracing) { tr_a += clock64() - w2; ++tr_c; }
           tc_fence_after();
           const uint32_t aaddr = smem_u32(smem + s * Cfg::kStageBytes);
           const uint32_t baddr = aaddr + Cfg::kABytes;
@@ -155,6 +164,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   } else {
     // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
     const int q = warp & 3;
+    const uint64_t store_pol = l2_policy_evict_first();
     uint8_t* wbuf = smem + Cfg::kEpiOffset + (warp - 2) * 2 * kEpiBufBytes;
     int uses = 0;
     const uint32_t accempty_leader = mapa_shared(smem_u32(accempty), 0);
@@ -167,21 +177,35 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
       const int b = local & 1;
       const uint32_t aph = (local >> 1) & 1;
+      const long long w3 = tracing ? clock64() : 0;
       if (!mbar_wait(&accfull[b], aph, wc, 15)) break;
+      const long long w4 = tracing ? clock64() : 0;
+      if (tracing) tr_a += w4 - w3;
       tc_fence_after();
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * 256;
-      epilogue_tile<OUT, TN>(tbase, &tmC, tn * TN, tm * TM + static_cast<int>(rank) * 128 + q * 32, alpha, wbuf,
-                             uses, lane, [&] {
-                               tc_fence_before();
-                               __syncwarp();
-                               if (lane == 0) mbar_arrive_cluster(accempty_leader + b * 8);
-                             });
+      auto release = [&] {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(accempty_leader + b * 8);
+      };
+      const int row0 = tm * TM + static_cast<int>(rank) * 128 + q * 32;
+      if constexpr (DIRECT_EPI) epilogue_tile_direct<OUT, TN>(tbase, p, row0 + lane, tn * TN, alpha, release);
+      else epilogue_tile<OUT, TN>(tbase, &tmC, tn * TN, row0, alpha, wbuf, uses, lane, store_pol,
+                                  (p.hints & 2) != 0, release);
+      if (tracing) { tr_b += clock64() - w4; ++tr_c; }
     }
     if (lane == 0) bulk_wait_group<0>();
   }
 
+  if (tracing && lane == 0) {
+    unsigned long long* tr = p.trace + static_cast<size_t>(blockIdx.x) * kTraceWords;
+    if (warp == 0) tr[3] = tr_a;
+    if (warp == 1 && leader) { tr[1] = tr_a; tr[2] = tr_b; tr[7] = tr_c; }
+    if (warp == 2) { tr[4] = tr_a; tr[5] = tr_b; tr[6] = tr_c; }
+  }
   tc_fence_before();
   cluster_sync();
+  if (tracing && threadIdx.x == 0) p.trace[static_cast<size_t>(blockIdx.x) * kTraceWords] = clock64() - t_start;
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();

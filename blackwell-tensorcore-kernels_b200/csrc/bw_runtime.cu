@@ -19,6 +19,8 @@ DeviceState g_dev[kMaxDevices];
 std::mutex g_mu;
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 unsigned long long g_budget_ns = 2000000000ull;
+unsigned long long* g_trace = nullptr;
+int g_trace_ctas = 0;
 bool g_budget_from_env = false;
 }  // namespace
 
@@ -34,6 +36,10 @@ int set_error(int code, const char* fmt, ...) {
 
 int cuda_error(cudaError_t e, const char* what) {
   return set_error(BW_ERR_CUDA, "%s failed: %s", what, cudaGetErrorString(e));
+}
+
+unsigned long long* trace_buffer(int ctas_needed) {
+  return (g_trace && ctas_needed <= g_trace_ctas) ? g_trace : nullptr;
 }
 
 unsigned long long wait_budget_ns() {
@@ -156,6 +162,13 @@ int bw_device_status(void* stream, int* out_status) {
   BW_CUDA(cudaMemset(d->status, 0, sizeof(int)));
   *out_status = v;
   if (v != 0) return set_error(BW_ERR_TIMEOUT, "kernel wait budget expired at site %d", v & 255);
+  return BW_OK;
+}
+
+int bw_set_trace_buffer(unsigned long long* dev_buf, int max_ctas) {
+  if (dev_buf && max_ctas <= 0) return set_error(BW_ERR_INVALID, "max_ctas must be > 0");
+  g_trace = dev_buf;
+  g_trace_ctas = dev_buf ? max_ctas : 0;
   return BW_OK;
 }
 

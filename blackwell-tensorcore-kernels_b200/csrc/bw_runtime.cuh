@@ -32,6 +32,7 @@ struct DeviceState {
 // Ensures the current device is initialised; returns BW_OK or an error status.
 int ensure_device(DeviceState** out);
 unsigned long long wait_budget_ns();
+unsigned long long* trace_buffer(int ctas_needed);  // null unless bw_set_trace_buffer armed one
 
 // 2-D row-major tensor map: dims {inner, outer}, box {box_inner, box_outer}, 128B swizzle.
 int make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner, uint64_t outer,

@@ -68,6 +68,13 @@ int bw_num_sms(int device);
 /* Reads (after synchronising `stream`) and clears the device status word that kernels
  * set when a bounded wait expires: 0 = ok, else (BW_ERR_TIMEOUT << 8) | site. */
 int bw_device_status(void* stream, int* out_status);
+/* Arms (dev_buf != NULL) or disarms the wait-time trace: every later CTA-pair GEMM launch
+ * with at most max_ctas CTAs writes 8 unsigned long long per CTA into dev_buf (device
+ * memory owned by the caller): [0] kernel cycles, [1] MMA-thread cycles waiting for loaded
+ * k-slabs, [2] MMA-thread cycles waiting for a free accumulator, [3] producer cycles
+ * waiting for free slabs, [4] epilogue cycles waiting for a finished accumulator,
+ * [5] epilogue busy cycles, [6] tiles, [7] k-slabs. Diagnostic; no reference counterpart. */
+int bw_set_trace_buffer(unsigned long long* dev_buf, int max_ctas);
 /* Overrides the per-wait budget of every kernel (nanoseconds; default 2e9). */
 int bw_set_wait_budget_ns(unsigned long long ns);
 
