@@ -74,6 +74,7 @@ def lib():
         "bw_gemm_fp4": [P, P, P, P, P, I, I, I, I, P],
         "bw_quantize_f16": [P, P, LL, P],
         "bw_quantize_fp8": [P, P, P, I, I, I, I, P],
+        "bw_quantize_fp8_noalloc": [P, P, P, I, I, I, I, P],
         "bw_quantize_fp4": [P, P, P, I, I, I, I, I, P],
         "bw_quantize_mxfp4": [P, P, P, I, I, I, I, P],
         "bw_unshard_columns": [P, P, I, I, I, P],
@@ -211,6 +212,22 @@ def quantize_fp8(src, transpose=False, scale_mode=SCALE_AMAX, dst=None, scale_ou
         scale_out = torch.empty(1, dtype=torch.float32, device=src.device)
     _check(lib().bw_quantize_fp8(_ptr(src), _ptr(dst), _ptr(scale_out), rows, cols, int(transpose), scale_mode,
                                  _stream(stream)))
+    return dst, scale_out
+
+
+def quantize_fp8_noalloc(src, transpose=False, scale_mode=SCALE_AMAX, dst=None, scale_out=None, stream=None):
+    """bw_quantize_fp8 through the entry point that allocates nothing (fixed library scratch).
+    `dst` and `scale_out` must be supplied by callers that cannot allocate; the defaults here
+    allocate them with torch for convenience."""
+    import torch
+
+    rows, cols = src.shape
+    if dst is None:
+        dst = torch.empty((cols, rows) if transpose else (rows, cols), dtype=torch.uint8, device=src.device)
+    if scale_out is None:
+        scale_out = torch.empty(1, dtype=torch.float32, device=src.device)
+    _check(lib().bw_quantize_fp8_noalloc(_ptr(src), _ptr(dst), _ptr(scale_out), rows, cols, int(transpose),
+                                         scale_mode, _stream(stream)))
     return dst, scale_out
 
 

@@ -334,3 +334,140 @@ int bw_unshard_columns(const float* C_shardmajor, float* C_rowmajor, int M, int 
 }
 
 }  // extern "C"
+
+// =========================================================================================
+// bw_quantize_fp8_noalloc: the per-tensor E4M3 quantiser for callers that cannot allocate
+// device memory. Some callers are not allowed to call cudaMalloc at all: code running in a
+// stream callback (CUDA forbids runtime API calls there), plugins hosted by a framework whose
+// own allocator has already reserved the device memory and must account for every byte, and
+// serving loops with a no-allocation latency contract. bw_quantize_fp8 needs a small device
+// workspace for its amax reduction, which the library cudaMallocs on a device's first use;
+// this variant keeps that scratch in a fixed array compiled into the library instead.
+//
+// Scratch: kNoAllocAmaxBlocks per-block maxima plus one result word, 64 KiB + 4 B in total,
+// held by every device that loads the library until the process exits. One block reduces
+// kNoAllocChunk input elements, so an input may hold at most
+// kNoAllocAmaxBlocks * kNoAllocChunk = 134,217,728 elements; larger inputs are rejected with
+// BW_ERR_INVALID before anything is launched. Every slot a call reads is written earlier in
+// the same call, so nothing has to be cleared between calls. All calls on a device share the
+// array: two calls whose kernels may overlap on the GPU (different streams without ordering)
+// race on it and must be serialised by the caller.
+//
+// Set-up: the first call on each device looks up the array's device address with
+// cudaGetSymbolAddress while that device is current (the array's name in host code is a host
+// stand-in, not a device address). Make that first call outside any stream capture.
+// Results are bit-identical to bw_quantize_fp8 (max is exact and order-independent).
+// =========================================================================================
+namespace bw {
+namespace {
+
+constexpr int kNoAllocAmaxBlocks = 16384;
+constexpr int kNoAllocChunk = 8192;  // elements reduced by one block (32 per thread)
+static __device__ __align__(256) unsigned g_noalloc_amax_scratch[kNoAllocAmaxBlocks + 1];
+
+void* g_noalloc_scratch_addr[64] = {};
+int g_noalloc_sms[64] = {};
+
+__global__ void k_amax_partial(const float* __restrict__ src, long long n, unsigned* __restrict__ partial) {
+  const long long base = static_cast<long long>(blockIdx.x) * kNoAllocChunk;
+  float m = 0.f;
+  for (int i = threadIdx.x; i < kNoAllocChunk; i += kQThreads) {
+    const long long j = base + i;
+    if (j < n) m = fmaxf(m, fabsf(src[j]));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  __shared__ float wm[kQThreads / 32];
+  if ((threadIdx.x & 31) == 0) wm[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < kQThreads / 32; ++w) m = fmaxf(m, wm[w]);
+    partial[blockIdx.x] = __float_as_uint(m);
+  }
+}
+
+__global__ void k_amax_final(const unsigned* __restrict__ partial, int nblocks, unsigned* __restrict__ out) {
+  float m = 0.f;
+  for (int i = threadIdx.x; i < nblocks; i += kQThreads) m = fmaxf(m, __uint_as_float(partial[i]));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  __shared__ float wm[kQThreads / 32];
+  if ((threadIdx.x & 31) == 0) wm[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < kQThreads / 32; ++w) m = fmaxf(m, wm[w]);
+    *out = __float_as_uint(m);
+  }
+}
+
+__global__ void k_store_one(float* out) { *out = 1.f; }
+
+// Once per device, with that device current: device address of the scratch array and the SM
+// count (neither call allocates).
+int noalloc_setup(int dev, unsigned** scratch, int* sms) {
+  if (dev < 0 || dev >= 64) return set_error(BW_ERR_INVALID, "device index %d out of range", dev);
+  if (!g_noalloc_scratch_addr[dev]) {
+    void* ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_amax_scratch);
+    if (e != cudaSuccess || !ptr) return cuda_error(e, "cudaGetSymbolAddress(no-alloc scratch)");
+    int n = 0;
+    BW_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+    g_noalloc_sms[dev] = n > 0 ? n : 1;
+    g_noalloc_scratch_addr[dev] = ptr;
+  }
+  *scratch = static_cast<unsigned*>(g_noalloc_scratch_addr[dev]);
+  *sms = g_noalloc_sms[dev];
+  return BW_OK;
+}
+
+}  // namespace
+}  // namespace bw
+
+extern "C" int bw_quantize_fp8_noalloc(const float* src, uint8_t* dst, float* scale_out, int rows, int cols,
+                                       int transpose, int scale_mode, void* stream) {
+  using namespace bw;
+  if (rows < 0 || cols < 0) return set_error(BW_ERR_INVALID, "negative size");
+  if (scale_mode != BW_SCALE_NONE && scale_mode != BW_SCALE_FIXED8 && scale_mode != BW_SCALE_AMAX)
+    return set_error(BW_ERR_INVALID, "bad scale_mode %d", scale_mode);
+  const long long n = static_cast<long long>(rows) * cols;
+  const long long limit = static_cast<long long>(kNoAllocAmaxBlocks) * kNoAllocChunk;
+  if (n > limit)
+    return set_error(BW_ERR_INVALID,
+                     "bw_quantize_fp8_noalloc: %lld elements exceed its fixed scratch limit of %lld elements "
+                     "(use bw_quantize_fp8)",
+                     n, limit);
+  if (n > 0 && (!src || !dst)) return set_error(BW_ERR_INVALID, "null src/dst");
+  int dev = 0;
+  BW_CUDA(cudaGetDevice(&dev));
+  unsigned* scratch = nullptr;
+  int sms = 1;
+  int r = noalloc_setup(dev, &scratch, &sms);
+  if (r != BW_OK) return r;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  unsigned* amax = scratch + kNoAllocAmaxBlocks;  // result word, written before it is read
+  if (n == 0) {
+    if (scale_out) {
+      k_store_one<<<1, 1, 0, s>>>(scale_out);
+      BW_CUDA(cudaGetLastError());
+    }
+    return BW_OK;
+  }
+  if (scale_mode == BW_SCALE_AMAX) {
+    const int nblocks = static_cast<int>((n + kNoAllocChunk - 1) / kNoAllocChunk);
+    k_amax_partial<<<nblocks, kQThreads, 0, s>>>(src, n, scratch);
+    BW_CUDA(cudaGetLastError());
+    k_amax_final<<<1, kQThreads, 0, s>>>(scratch, nblocks, amax);
+    BW_CUDA(cudaGetLastError());
+  }
+  if (transpose) {
+    dim3 grid((cols + 31) / 32, (rows + 63) / 64);
+    k_quant_transpose<0><<<grid, kQThreads, 0, s>>>(src, dst, rows, cols, scale_mode, 448.f, amax, scale_out);
+  } else {
+    long long g = (n + kQThreads - 1) / kQThreads;
+    if (g > static_cast<long long>(sms) * 16) g = static_cast<long long>(sms) * 16;
+    k_quant_rowmajor<0><<<static_cast<int>(g), kQThreads, 0, s>>>(src, dst, rows, cols, scale_mode, 448.f, amax,
+                                                                   scale_out);
+  }
+  BW_CUDA(cudaGetLastError());
+  return BW_OK;
+}

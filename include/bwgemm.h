@@ -119,6 +119,18 @@ int bw_quantize_fp8(const float* src, uint8_t* dst, float* scale_out, int rows, 
  * NaN -> +0). Packed containers pair values along the contiguous dimension of dst. */
 int bw_quantize_fp4(const float* src, uint8_t* dst, float* scale_out, int rows, int cols, int transpose,
                     int scale_mode, int container, void* stream);
+/* bw_quantize_fp8 for callers that cannot allocate device memory (no counterpart in the
+ * reference). Stream callbacks may not call the CUDA runtime, framework-hosted plugins may
+ * find the device memory already reserved by the host's own allocator, and latency-bound
+ * serving loops may forbid allocation; bw_quantize_fp8 needs a small library-allocated
+ * workspace for its amax reduction, this variant uses a fixed scratch array compiled into the
+ * library (64 KiB per device, held until exit) and calls no allocating routine. Same
+ * arguments and bit-identical results. Limit: rows * cols <= 134,217,728 elements, larger
+ * inputs return BW_ERR_INVALID. The first call on each device looks the array up (make it
+ * outside any stream capture). Calls share the array: calls that may overlap on the GPU
+ * (unordered streams) race and must be serialised by the caller. */
+int bw_quantize_fp8_noalloc(const float* src, uint8_t* dst, float* scale_out, int rows, int cols, int transpose,
+                            int scale_mode, void* stream);
 /* Packed E2M1 plus UE8M0 scale factors along the contiguous (K) dimension of dst.
  * dst is (transpose ? cols : rows) x (K/2) where K = (transpose ? rows : cols); sf receives
  * bw_sf_bytes(outer, K) bytes in the tiled layout. */
