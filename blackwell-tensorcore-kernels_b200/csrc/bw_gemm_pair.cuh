@@ -20,10 +20,11 @@
 
 namespace bw {
 
-template <Kind KIND, int STAGES, bool DIRECT_EPI = false>
+template <Kind KIND, int STAGES, bool DIRECT_EPI = false, int KSUB = 1>
 struct PairCfg {
-  static constexpr int kABytes = 128 * kSlabBytes;  // this CTA's 128 rows of A
-  static constexpr int kBBytes = 128 * kSlabBytes;  // this CTA's 128 columns of B
+  static constexpr int kAtomBytes = 128 * kSlabBytes;  // 128 rows x one 128-byte swizzle atom of K
+  static constexpr int kABytes = KSUB * kAtomBytes;    // this CTA's 128 rows of A, KSUB atoms of K
+  static constexpr int kBBytes = KSUB * kAtomBytes;    // this CTA's 128 columns of B
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kEpiOffset = STAGES * kStageBytes;
   static constexpr int kBarOffset = kEpiOffset + (DIRECT_EPI ? 0 : kEpiBytes);
@@ -33,13 +34,13 @@ struct PairCfg {
   static constexpr int kTmemCols = 512;  // two 256-column FP32 accumulators
 };
 
-template <Kind KIND, bool B_MN, int STAGES, Out OUT, bool DIRECT_EPI>
+template <Kind KIND, bool B_MN, int STAGES, Out OUT, bool DIRECT_EPI, int KSUB>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     bw_tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                            const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
-  using Cfg = PairCfg<KIND, STAGES, DIRECT_EPI>;
-  constexpr int KX = KindTraits<KIND>::kCoordPerSlab;
-  constexpr int KE = KindTraits<KIND>::kElemsPerSlab;
+  using Cfg = PairCfg<KIND, STAGES, DIRECT_EPI, KSUB>;
+  constexpr int KX = KindTraits<KIND>::kCoordPerSlab;          // tensor-map units per swizzle atom
+  constexpr int KE = KindTraits<KIND>::kElemsPerSlab * KSUB;   // K elements per pipeline stage
   constexpr int TM = 256, TN = 256;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -103,12 +104,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           uint8_t* sB = sA + Cfg::kABytes;
           if (leader) mbar_arrive_expect_tx(&full[s], 2 * Cfg::kStageBytes);
           const uint32_t fb = full_leader + s * 8;
-          tma_load_2d_pair(&tmA, fb, sA, kb * KX, arow, pol);
-          if constexpr (B_MN) {
-            tma_load_2d_pair(&tmB, fb, sB, bcol, kb * 64, pol);
-            tma_load_2d_pair(&tmB, fb, sB + 64 * kSlabBytes, bcol + 64, kb * 64, pol);
-          } else {
-            tma_load_2d_pair(&tmB, fb, sB, kb * KX, bcol, pol);
+#pragma unroll
+          for (int j = 0; j < KSUB; ++j) {
+            const int ka = kb * KSUB + j;  // swizzle-atom index along K
+            tma_load_2d_pair(&tmA, fb, sA + j * Cfg::kAtomBytes, ka * KX, arow, pol);
+            if constexpr (B_MN) {
+              tma_load_2d_pair(&tmB, fb, sB + j * Cfg::kAtomBytes, bcol, ka * 64, pol);
+              tma_load_2d_pair(&tmB, fb, sB + j * Cfg::kAtomBytes + 64 * kSlabBytes, bcol + 64, ka * 64, pol);
+            } else {
+              tma_load_2d_pair(&tmB, fb, sB + j * Cfg::kAtomBytes, ka * KX, bcol, pol);
+            }
           }
           if (++s == STAGES) { s = 0; ph ^= 1; }
         }
@@ -140,12 +145,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const uint32_t aaddr = smem_u32(smem + s * Cfg::kStageBytes);
           const uint32_t baddr = aaddr + Cfg::kABytes;
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
-            const uint64_t adesc = sdesc_sw128(aaddr + k * 32, 16, 1024);
+          for (int kk = 0; kk < 4 * KSUB; ++kk) {
+            const int j = kk >> 2, k = kk & 3;
+            const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
+            const uint64_t adesc = sdesc_sw128(aaddr + j * Cfg::kAtomBytes + k * 32, 16, 1024);
             uint64_t bdesc;
-            if constexpr (B_MN) bdesc = sdesc_sw128(baddr + k * 16 * kSlabBytes, 64 * kSlabBytes, 1024);
-            else bdesc = sdesc_sw128(baddr + k * 32, 16, 1024);
+            if constexpr (B_MN)
+              bdesc = sdesc_sw128(baddr + j * Cfg::kAtomBytes + k * 16 * kSlabBytes, 64 * kSlabBytes, 1024);
+            else bdesc = sdesc_sw128(baddr + j * Cfg::kAtomBytes + k * 32, 16, 1024);
             if constexpr (KIND == Kind::F16) umma_f16_pair(d_tmem, adesc, bdesc, idesc, acc);
             else umma_f8f6f4_pair(d_tmem, adesc, bdesc, idesc, acc);
           }

@@ -251,3 +251,31 @@ def test_unshard_columns(cuda_dev):
     out = bwgemm.unshard_columns(_t(np.ascontiguousarray(shards), cuda_dev), M, N, world)
     torch.cuda.synchronize()
     assert np.array_equal(_np(out), full)
+
+
+@pytest.mark.parametrize("kind", ["f16", "fp8"])
+def test_pair_kernel_staged_epilogue_when_c_not_32b_aligned(cuda_dev, kind):
+    """C only 16-byte aligned selects the shared-memory/TMA-store epilogue of the CTA-pair
+    kernel instead of the direct 32-byte stores; results must be identical."""
+    import torch
+
+    M = N = K = 2048
+    if kind == "f16":
+        A = _f16(o.seeded_uniform((M, K), 61))
+        B = _f16(o.seeded_uniform((K, N), 62))
+        Ad, Bd = _t(A, cuda_dev).half(), _t(B, cuda_dev).half()
+        ref = bwgemm.gemm_f16(Ad, Bd)
+        buf = torch.empty(M * N + 4, dtype=torch.float32, device=cuda_dev)
+        C = buf[4:].view(M, N)  # 16-byte offset from a 256-byte aligned base
+        bwgemm.gemm_f16(Ad, Bd, C)
+    else:
+        qa, sa = bwgemm.quantize_fp8(_t(o.seeded_normal((M, K), 63), cuda_dev), False)
+        qb, sb = bwgemm.quantize_fp8(_t(o.seeded_normal((K, N), 64), cuda_dev), True)
+        ref = bwgemm.gemm_fp8(qa, qb, sa, sb)
+        buf = torch.empty(M * N + 8, dtype=torch.bfloat16, device=cuda_dev)
+        C = buf[8:].view(M, N)
+        bwgemm.gemm_fp8(qa, qb, sa, sb, C)
+    torch.cuda.synchronize()
+    _status_ok()
+    assert C.data_ptr() % 32 == 16
+    assert torch.equal(C, ref)
