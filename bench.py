@@ -346,8 +346,11 @@ def run_ours(args, world, rank, local):
 
 
 def compare_rows(args, wl, inp, dev, stream):
-    """Library rows measured in the same run (cuBLAS / cuBLASLt through torch) and our other
-    precisions; each timed like the headline (warm-up, CUDA events, 20 launches)."""
+    """Library rows measured in the same run (cuBLAS / cuBLASLt through torch) against ours.
+    Each pair is timed in interleaved blocks of equal length (ours, library, ours, ...), so
+    both see the same power / clock state; the medians over blocks are reported."""
+    import statistics
+
     import torch
 
     import bwgemm
@@ -355,29 +358,41 @@ def compare_rows(args, wl, inp, dev, stream):
     M = N = K = DIM
     flops = 2.0 * M * N * K
     out = {}
+    block = max(10, min(args.steps, 50))
 
-    def tf(fn, n=20):
-        ms = timed_steps(fn, n, 3, 1, stream)
-        return round(flops / (ms * 1e-3) / 1e12, 1)
+    def tf(fn):
+        ms = timed_steps(fn, block, 2, 1, stream)
+        return flops / (ms * 1e-3) / 1e12
+
+    def interleaved(name_a, fa, name_b, fb, rounds=4):
+        ra, rb = [], []
+        for _ in range(rounds):
+            ra.append(tf(fa))
+            rb.append(tf(fb))
+        out[name_a] = round(statistics.median(ra), 1)
+        out[name_b] = round(statistics.median(rb), 1)
 
     try:
         if wl == "f16":
             A, B = inp["A"], inp["B"]
-            out["cublas_f16_f32out_tflops"] = tf(lambda: torch.mm(A, B, out_dtype=torch.float32))
-            out["cublas_f16_f16out_tflops"] = tf(lambda: torch.mm(A, B))
+            C = torch.empty((M, N), dtype=torch.float32, device=dev)
+            interleaved("ours_f16_f32out_tflops", lambda: bwgemm.gemm_f16(A, B, C, stream=stream),
+                        "cublas_f16_f32out_tflops", lambda: torch.mm(A, B, out_dtype=torch.float32))
             A32 = (A.float() * 2)
             B32 = (B.float() * 2)
             qa, sa = bwgemm.quantize_fp8(A32, False, bwgemm.SCALE_AMAX)
             qb, sb = bwgemm.quantize_fp8(B32, True, bwgemm.SCALE_AMAX)
             C8 = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
-            out["ours_fp8_bf16out_tflops"] = tf(lambda: bwgemm.gemm_fp8(qa, qb, sa, sb, C8, stream=stream))
             a8 = qa.view(torch.float8_e4m3fn)
             b8 = qb.view(torch.float8_e4m3fn).t()
-            out["cublaslt_fp8_bf16out_tflops"] = tf(
-                lambda: torch._scaled_mm(a8, b8, scale_a=sa, scale_b=sb, out_dtype=torch.bfloat16))
+            interleaved("ours_fp8_bf16out_tflops", lambda: bwgemm.gemm_fp8(qa, qb, sa, sb, C8, stream=stream),
+                        "cublaslt_fp8_bf16out_tflops",
+                        lambda: torch._scaled_mm(a8, b8, scale_a=sa, scale_b=sb, out_dtype=torch.bfloat16))
             q4a, sfa = bwgemm.quantize_mxfp4(A32, False, bwgemm.MX_BLOCK32)
             q4b, sfb = bwgemm.quantize_mxfp4(B32, True, bwgemm.MX_BLOCK32)
-            out["ours_mxfp4_bf16out_tflops"] = tf(lambda: bwgemm.gemm_mxfp4(q4a, q4b, sfa, sfb, K, C=C8, stream=stream))
+            out["ours_mxfp4_bf16out_tflops"] = round(
+                tf(lambda: bwgemm.gemm_mxfp4(q4a, q4b, sfa, sfb, K, C=C8, stream=stream)), 1)
+            out["block_steps"] = block
     except Exception as ex:  # a missing library path must not hide the headline number
         out["error"] = f"{type(ex).__name__}: {ex}"[:200]
     return out

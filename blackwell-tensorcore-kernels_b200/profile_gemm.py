@@ -1,0 +1,26 @@
+"""Small driver for profiling one GEMM kind under ncu: KIND=f16|fp8|mxfp4, N=size (square).
+Runs the GEMM three times (ncu -s 1 -c 1 then captures the second launch).
+
+    KIND=f16 N=8192 ncu --set full --clock-control none -k regex:bw_tc_gemm -s 1 -c 1 \
+        -o prof python blackwell-tensorcore-kernels_b200/profile_gemm.py
+"""
+import os
+import sys
+
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+import torch, bwgemm
+bwgemm.init(0)
+dev = torch.device('cuda:0')
+kind = os.environ.get('KIND', 'f16'); n = int(os.environ.get('N', '8192'))
+M = N = K = n
+if kind == 'f16':
+    A = torch.randn(M, K, device=dev).half(); B = torch.randn(K, N, device=dev).half(); C = torch.empty(M, N, device=dev)
+    f = lambda: bwgemm.gemm_f16(A, B, C)
+elif kind == 'fp8':
+    qa, sa = bwgemm.quantize_fp8(torch.randn(M, K, device=dev)); qb, sb = bwgemm.quantize_fp8(torch.randn(K, N, device=dev), True)
+    C = torch.empty(M, N, device=dev, dtype=torch.bfloat16); f = lambda: bwgemm.gemm_fp8(qa, qb, sa, sb, C)
+else:
+    qa, sfa = bwgemm.quantize_mxfp4(torch.randn(M, K, device=dev)); qb, sfb = bwgemm.quantize_mxfp4(torch.randn(K, N, device=dev), True)
+    C = torch.empty(M, N, device=dev, dtype=torch.bfloat16); f = lambda: bwgemm.gemm_mxfp4(qa, qb, sfa, sfb, K, C=C)
+for _ in range(3): f()
+torch.cuda.synchronize(); print('ok', bwgemm.device_status())
