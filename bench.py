@@ -181,15 +181,18 @@ def make_inputs(workload: str, rank: int, dev):
     """Seeded synthetic inputs of the BASELINE shapes (per rank: its own column shard)."""
     import torch
 
-    g = torch.Generator(device=dev)
-    g.manual_seed(1234 + 17 * rank)
+    # A is the same on every rank (replicated); B is this rank's column shard of the full B.
+    ga = torch.Generator(device=dev)
+    ga.manual_seed(1234)
+    gb = torch.Generator(device=dev)
+    gb.manual_seed(4321 + 17 * rank)
     M = N = K = DIM
     if workload == "f16":
-        A = (torch.rand((M, K), generator=g, device=dev) * 2 - 1).half()
-        B = (torch.rand((K, N), generator=g, device=dev) * 2 - 1).half()
+        A = (torch.rand((M, K), generator=ga, device=dev) * 2 - 1).half()
+        B = (torch.rand((K, N), generator=gb, device=dev) * 2 - 1).half()
         return {"A": A, "B": B}
-    A32 = torch.randn((M, K), generator=g, device=dev)
-    B32 = torch.randn((K, N), generator=g, device=dev)
+    A32 = torch.randn((M, K), generator=ga, device=dev)
+    B32 = torch.randn((K, N), generator=gb, device=dev)
     return {"A32": A32, "B32": B32}
 
 
@@ -268,6 +271,24 @@ def run_ours(args, world, rank, local):
     status = bwgemm.device_status()
     if status != 0:
         raise SystemExit(f"kernel reported status {status}")
+    gather = None
+    if args.gather and world > 1:
+        # untimed by the headline: NCCL all-gather of the C shards into row-major M x (N world)
+        import sharding
+
+        torch.cuda.synchronize()
+        barrier(world)
+        g0 = torch.cuda.Event(enable_timing=True)
+        g1 = torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        full = sharding.gather_columns(C, world)
+        g1.record(stream)
+        torch.cuda.synchronize()
+        gms = max_over_ranks(g0.elapsed_time(g1), world)
+        ok = bool(torch.equal(full[:, rank * N:(rank + 1) * N], C))
+        gather = {"ms": round(gms, 3), "bytes_per_rank": int(C.numel() * C.element_size() * (world - 1)),
+                  "layout": "row-major M x N after bw_unshard_columns", "own_shard_intact": ok}
+        del full
     value = world * flops / (ms * 1e-3) / 1e12
 
     # ---- e2e: pinned host inputs -> device, GEMM through the C ABI, C -> pinned host
@@ -332,6 +353,7 @@ def run_ours(args, world, rank, local):
         "e2e": e2e,
         "roofline": roofline,
         "gpu_launches": args.steps,
+        "gather": gather,
         "clocks": clk,
         "impl": "ours",
     }
