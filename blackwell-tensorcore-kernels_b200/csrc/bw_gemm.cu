@@ -4,6 +4,7 @@
 
 #include "bw_gemm_kernel.cuh"
 #include "bw_gemm_pair.cuh"
+#include "bw_gemm_pair_mx.cuh"
 #include "bw_runtime.cuh"
 
 namespace bw {
@@ -99,6 +100,44 @@ bool use_pair(int M, int N, const DeviceState& d) {
   if (forced == 1) return true;
   const long tiles = static_cast<long>((M + 255) / 256) * ((N + 255) / 256);
   return tiles >= d.sms / 2;
+}
+
+template <Out OUT>
+int launch_pair_mx(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tsa, const CUtensorMap& tsb,
+                   GemmParams p, cudaStream_t stream, const DeviceState& d) {
+  auto kern = bw_tc_gemm_pair_mx_kernel<OUT>;
+  static bool attr_done[64] = {};
+  static int max_clusters[64] = {};
+  int dev = 0;
+  BW_CUDA(cudaGetDevice(&dev));
+  if (!attr_done[dev & 63]) {
+    BW_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, MxPairCfg::kSmemBytes));
+    attr_done[dev & 63] = true;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (d.sms / 2), 1, 1);
+    cfg.blockDim = dim3(kMxThreads, 1, 1);
+    cfg.dynamicSmemBytes = MxPairCfg::kSmemBytes;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = d.sms / 2;
+    }
+    max_clusters[dev & 63] = n;
+  }
+  const int tiles = ((p.M + 255) / 256) * ((p.N + 255) / 256);
+  const int resident = max_clusters[dev & 63];
+  const int clusters = tiles < resident ? tiles : resident;
+  p.trace = nullptr;
+  kern<<<2 * clusters, kMxThreads, MxPairCfg::kSmemBytes, stream>>>(ta, tb, tsa, tsb, p);
+  BW_CUDA(cudaGetLastError());
+  return BW_OK;
 }
 
 // Output tensor map for the TMA-store epilogue: 32 rows x 128 B boxes, 128B swizzle.
@@ -241,6 +280,26 @@ int gemm_mxf4_impl(const uint8_t* A, const uint8_t* Bt, const uint8_t* sfa, cons
   p.sfa = sfa;
   p.sfb = sfb;
   p.sf_kgroups = ((K + 31) / 32 + 3) / 4;
+  const bool pair_ok = env_int("BW_MX_PAIR", 1) != 0 && use_pair(M, N, *d) &&
+                       (out_dtype == BW_OUT_BF16 || (reinterpret_cast<uintptr_t>(C) & 31u) == 0);
+  if (pair_ok) {
+    CUtensorMap ta2, tb2, tsa, tsb;
+    if ((r = make_tmap_2d(&ta2, CU_TENSOR_MAP_DATA_TYPE_UINT8, A, K / 2, M, uint64_t(K / 2), 128, 128)) != BW_OK) return r;
+    if ((r = make_tmap_2d(&tb2, CU_TENSOR_MAP_DATA_TYPE_UINT8, Bt, K / 2, N, uint64_t(K / 2), 128, 128)) != BW_OK) return r;
+    if (sfa) {
+      // scale factors seen as rows of 256 bytes; one box = 8 rows = 4 atoms of 512 B
+      const uint64_t ra = bw_sf_bytes(M, K) / 256, rb = bw_sf_bytes(N, K) / 256;
+      if ((r = make_tmap_2d(&tsa, CU_TENSOR_MAP_DATA_TYPE_UINT8, sfa, 256, ra, 256, 256, 8,
+                            CU_TENSOR_MAP_SWIZZLE_NONE)) != BW_OK) return r;
+      if ((r = make_tmap_2d(&tsb, CU_TENSOR_MAP_DATA_TYPE_UINT8, sfb, 256, rb, 256, 256, 8,
+                            CU_TENSOR_MAP_SWIZZLE_NONE)) != BW_OK) return r;
+    } else {
+      tsa = ta2;  // unused: plain FP4 keeps every block scale at 2^0
+      tsb = tb2;
+    }
+    if (out_dtype == BW_OUT_F32) return launch_pair_mx<Out::F32>(ta2, tb2, tsa, tsb, p, s, *d);
+    return launch_pair_mx<Out::BF16>(ta2, tb2, tsa, tsb, p, s, *d);
+  }
   if (out_dtype == BW_OUT_F32) return launch<Kind::MXF4, false, 128, 5, 2, Out::F32>(ta, tb, tc, p, s, *d);
   return launch<Kind::MXF4, false, 128, 5, 2, Out::BF16>(ta, tb, tc, p, s, *d);
 }

@@ -1,0 +1,258 @@
+// CTA-pair block-scaled FP4 GEMM (kind::mxf4, E2M1 packed, UE8M0 per 32 K): 256 x 256 tiles.
+//
+// Replaces gemm_lowprec_t<MXFP4> / <FP4> (src/gemm_mma_fp8.cu:89-223, 305-317) for large
+// problems. Structure as bw_tc_gemm_pair_kernel (bw_gemm_pair.cuh) with these differences:
+//   * every stage also carries the scale factors: each CTA loads the SF atoms of its own 128 A
+//     rows and of all 256 B rows of the tile (both CTAs' tensor cores scale the full N); the
+//     leader's MMA thread copies them to Tensor Memory with tcgen05.cp.cta_group::2 (each CTA
+//     from its own shared memory) before the stage's MMAs;
+//   * Tensor Memory holds one 256-column FP32 accumulator plus 48 scale-factor columns (two
+//     accumulators would leave no room), so 8 epilogue warps drain the accumulator into
+//     registers (128 columns each), release it at once and convert/store while the next tile
+//     already accumulates.
+// Stage = 2 K atoms (512 FP4 values): A 32 KB + B 32 KB + SFA 2 KB + SFB 4 KB per CTA, 3 stages.
+// With null scale-factor pointers (plain FP4, per-tensor scales only) the 0x7f-filled scale
+// slots are copied once and every block scale stays 2^0.
+#pragma once
+#include "bw_gemm_kernel.cuh"
+
+namespace bw {
+
+constexpr int kMxThreads = 320;  // producer, MMA, 8 epilogue warps
+constexpr int kMxKsub = 2;
+constexpr int kMxStages = 3;
+
+struct MxPairCfg {
+  static constexpr int kAtom = 128 * kSlabBytes;           // 128 rows x 128 B
+  static constexpr int kABytes = kMxKsub * kAtom;          // 32 KB
+  static constexpr int kBBytes = kMxKsub * kAtom;          // 32 KB
+  static constexpr int kSfaBytes = kMxKsub * 1024;         // 2 SF atoms (512 B) per K atom of 256
+  static constexpr int kSfbBytes = 2 * kSfaBytes;          // two 128-row blocks of B
+  static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;
+  static constexpr int kBarOffset = kMxStages * kStageBytes;
+  static constexpr int kNumBars = 2 * kMxStages + 2 + 1;  // full, empty, accfull, accempty, teardown
+  static constexpr int kSmemBytes = kBarOffset + kNumBars * 8 + 16 + 1024;
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
+  static constexpr int kSfaCols = 4 * kMxKsub * 2;          // 4 atoms per stage x 4 columns
+  static constexpr int kSfbCols = 2 * kSfaCols;             // two row blocks
+  static constexpr int kTmemCols = 512;                     // 256 accumulator + 48 SF, rounded up
+};
+
+template <Out OUT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
+    bw_tc_gemm_pair_mx_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                              const __grid_constant__ CUtensorMap tmSfa, const __grid_constant__ CUtensorMap tmSfb,
+                              const GemmParams p) {
+  using Cfg = MxPairCfg;
+  constexpr int KX = 128;    // packed bytes per K atom (256 FP4 values)
+  constexpr int KE = 256 * kMxKsub;
+  constexpr int TM = 256, TN = 256;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kBarOffset);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + kMxStages;
+  uint64_t* accfull = bars + 2 * kMxStages;
+  uint64_t* accempty = accfull + 1;
+  uint64_t* teardown = accfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::kNumBars);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const uint32_t peer = rank ^ 1u;
+  const bool leader = rank == 0;
+  const int cluster = blockIdx.x >> 1;
+  const int nclusters = gridDim.x >> 1;
+  const int tiles_m = (p.M + TM - 1) / TM;
+  const int tiles_n = (p.N + TN - 1) / TN;
+  const int num_tiles = tiles_m * tiles_n;
+  const int nk = (p.K + KE - 1) / KE;
+  const bool unit_sf = p.sfa == nullptr;
+  const WaitCtl wc{abort_flag, p.status, p.budget_ns};
+
+  // Scale-factor slots start at 2^0 (0x7f): the plain-FP4 path copies them once.
+  for (int s = 0; s < kMxStages; ++s) {
+    uint32_t* sf = reinterpret_cast<uint32_t*>(smem + s * Cfg::kStageBytes + Cfg::kABytes + Cfg::kBBytes);
+    for (int i = threadIdx.x; i < (Cfg::kSfaBytes + Cfg::kSfbBytes) / 4; i += kMxThreads) sf[i] = 0x7f7f7f7fu;
+  }
+  fence_proxy_async_smem();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kMxStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    mbar_init(accfull, 1);
+    mbar_init(accempty, 2 * 8);  // 8 epilogue warps in each CTA
+    mbar_init(teardown, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    if (!unit_sf) { tma_prefetch_desc(&tmSfa); tma_prefetch_desc(&tmSfb); }
+  }
+  if (warp == 1) { tmem_alloc_pair(tmem_slot, Cfg::kTmemCols); tmem_relinquish_pair(); }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t tmem_sfa = tmem_base + 256;
+  const uint32_t tmem_sfb = tmem_sfa + Cfg::kSfaCols;
+
+  if (warp == 0) {
+    // ---------------- TMA producer (both CTAs) ----------------
+    if (lane == 0) {
+      const uint64_t pol = l2_policy_evict_last();
+      const uint32_t full_leader = mapa_shared(smem_u32(full), 0);
+      const uint32_t stage_tx = unit_sf ? (Cfg::kABytes + Cfg::kBBytes) : Cfg::kStageBytes;
+      int s = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int t = cluster; t < num_tiles && ok; t += nclusters) {
+        int tm, tn;
+        tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
+        const int arow = tm * TM + static_cast<int>(rank) * 128;
+        const int bcol = tn * TN + static_cast<int>(rank) * 128;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&empty[s], ph ^ 1, wc, 31)) { ok = false; break; }
+          uint8_t* sA = smem + s * Cfg::kStageBytes;
+          uint8_t* sB = sA + Cfg::kABytes;
+          uint8_t* sSfa = sB + Cfg::kBBytes;
+          uint8_t* sSfb = sSfa + Cfg::kSfaBytes;
+          if (leader) mbar_arrive_expect_tx(&full[s], 2 * stage_tx);
+          const uint32_t fb = full_leader + s * 8;
+#pragma unroll
+          for (int j = 0; j < kMxKsub; ++j) {
+            const int ka = kb * kMxKsub + j;
+            tma_load_2d_pair(&tmA, fb, sA + j * Cfg::kAtom, ka * KX, arow, pol);
+            tma_load_2d_pair(&tmB, fb, sB + j * Cfg::kAtom, ka * KX, bcol, pol);
+          }
+          if (!unit_sf) {
+            // SF buffers viewed as rows of 256 B (an atom = 2 rows); a stage needs 4 atoms
+            // (k groups 4kb..4kb+3) of one row block: one 8-row box. Boxes past the end of a
+            // row block read the next block's scales for zero-filled K, past the buffer zeros.
+            const int kg0 = kb * 4;
+            tma_load_2d_pair(&tmSfa, fb, sSfa, 0, ((tm * 2 + static_cast<int>(rank)) * p.sf_kgroups + kg0) * 2, pol);
+            tma_load_2d_pair(&tmSfb, fb, sSfb, 0, ((tn * 2) * p.sf_kgroups + kg0) * 2, pol);
+            tma_load_2d_pair(&tmSfb, fb, sSfb + Cfg::kSfaBytes, 0, ((tn * 2 + 1) * p.sf_kgroups + kg0) * 2, pol);
+          }
+          if (++s == kMxStages) { s = 0; ph ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (leader only) ----------------
+    if (leader && lane == 0) {
+      const uint32_t empty_own = smem_u32(empty), empty_peer = mapa_shared(smem_u32(empty), peer);
+      const uint32_t accfull_own = smem_u32(accfull), accfull_peer = mapa_shared(smem_u32(accfull), peer);
+      int s = 0;
+      uint32_t ph = 0;
+      int local = 0;
+      bool ok = true;
+      bool sf_loaded = false;
+      for (int t = cluster; t < num_tiles && ok; t += nclusters, ++local) {
+        if (!mbar_wait(accempty, (local & 1) ^ 1, wc, 32)) { ok = false; break; }
+        tc_fence_after();
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&full[s], ph, wc, 33)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t aaddr = smem_u32(smem + s * Cfg::kStageBytes);
+          const uint32_t baddr = aaddr + Cfg::kABytes;
+          const uint32_t sfa_s = baddr + Cfg::kBBytes;
+          const uint32_t sfb_s = sfa_s + Cfg::kSfaBytes;
+          if (!unit_sf || !sf_loaded) {
+            // SFA: 4 atoms -> columns [4a, 4a+4); SFB: atom a of row block rb -> 8a + 4rb.
+#pragma unroll
+            for (int a = 0; a < 4; ++a) {
+              tmem_cp_32x128b_warpx4_pair(tmem_sfa + 4 * a, sdesc_noswz(sfa_s + 512 * a, 16, 128));
+              tmem_cp_32x128b_warpx4_pair(tmem_sfb + 8 * a, sdesc_noswz(sfb_s + 512 * a, 16, 128));
+              tmem_cp_32x128b_warpx4_pair(tmem_sfb + 8 * a + 4,
+                                          sdesc_noswz(sfb_s + Cfg::kSfaBytes + 512 * a, 16, 128));
+            }
+            sf_loaded = true;
+          }
+#pragma unroll
+          for (int kk = 0; kk < 4 * kMxKsub; ++kk) {
+            const int j = kk >> 2, k = kk & 3;
+            const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
+            const uint64_t adesc = sdesc_sw128(aaddr + j * Cfg::kAtom + k * 32, 16, 1024);
+            const uint64_t bdesc = sdesc_sw128(baddr + j * Cfg::kAtom + k * 32, 16, 1024);
+            // MMA kk covers 64 K values = SF blocks 2kk, 2kk+1: atom kk/2, byte (2kk) % 4.
+            const uint32_t sf_id = (2 * kk) & 3;
+            const uint32_t atom = unit_sf ? 0u : static_cast<uint32_t>(kk >> 1);
+            umma_mxf4_pair(tmem_base, adesc, bdesc, idesc_mxf4(256, 256, sf_id, sf_id), tmem_sfa + 4 * atom,
+                           tmem_sfb + 8 * atom, acc);
+          }
+          umma_commit_pair(empty_own + s * 8);
+          umma_commit_pair(empty_peer + s * 8);
+          if (++s == kMxStages) { s = 0; ph ^= 1; }
+        }
+        if (ok) {
+          umma_commit_pair(accfull_own);
+          umma_commit_pair(accfull_peer);
+        }
+      }
+      umma_commit_pair(smem_u32(teardown));
+      mbar_wait(teardown, 0, wc, 34);
+    }
+  } else {
+    // ---------------- epilogue: warps 2..9, lane quarter q, column half h ----------------
+    const int q = warp & 3;
+    const int h = (warp - 2) >> 2;
+    const uint32_t accempty_leader = mapa_shared(smem_u32(accempty), 0);
+    float alpha = 1.f;
+    if (p.scale_a) alpha *= __ldg(p.scale_a);
+    if (p.scale_b) alpha *= __ldg(p.scale_b);
+    int local = 0;
+    for (int t = cluster; t < num_tiles; t += nclusters, ++local) {
+      int tm, tn;
+      tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
+      if (!mbar_wait(accfull, local & 1, wc, 35)) break;
+      tc_fence_after();
+      uint32_t r[128];
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + h * 128;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(tbase + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&r[32 * c]));
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(accempty_leader);  // accumulator free: next tile may start
+      const int row = tm * TM + static_cast<int>(rank) * 128 + q * 32 + lane;
+      if (row < p.M) {
+        const int col0 = tn * TN + h * 128;
+#pragma unroll
+        for (int g = 0; g < 16; ++g) {  // 16 groups of 8 columns
+          const int col = col0 + 8 * g;
+          if (col >= p.N) break;
+          if constexpr (OUT == Out::F32) {
+            float* dst = reinterpret_cast<float*>(p.C) + static_cast<size_t>(row) * p.ldc + col;
+            uint32_t v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = __float_as_uint(__uint_as_float(r[8 * g + j]) * alpha);
+            st_global_v8(dst, v);
+          } else {
+            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.C) + static_cast<size_t>(row) * p.ldc + col;
+            uint32_t v[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              __nv_bfloat162 b2 = __floats2bfloat162_rn(__uint_as_float(r[8 * g + 2 * j]) * alpha,
+                                                        __uint_as_float(r[8 * g + 2 * j + 1]) * alpha);
+              v[j] = *reinterpret_cast<uint32_t*>(&b2);
+            }
+            *reinterpret_cast<uint4*>(dst) = make_uint4(v[0], v[1], v[2], v[3]);
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+}  // namespace bw

@@ -36,7 +36,8 @@ unsigned long long* trace_buffer(int ctas_needed);  // null unless bw_set_trace_
 
 // 2-D row-major tensor map: dims {inner, outer}, box {box_inner, box_outer}, 128B swizzle.
 int make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner, uint64_t outer,
-                 uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer);
+                 uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+                 CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B);
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 

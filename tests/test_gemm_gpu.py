@@ -279,3 +279,50 @@ def test_pair_kernel_staged_epilogue_when_c_not_32b_aligned(cuda_dev, kind):
     _status_ok()
     assert C.data_ptr() % 32 == 16
     assert torch.equal(C, ref)
+
+
+MX_PAIR_SHAPES = [(512, 512, 512), (300, 520, 1024), (1024, 768, 800), (2048, 2048, 4096)]
+
+
+@pytest.mark.parametrize("M,N,K", MX_PAIR_SHAPES)
+@pytest.mark.parametrize("out", [bwgemm.OUT_F32, bwgemm.OUT_BF16])
+def test_mxfp4_pair_kernel_parity(cuda_dev, monkeypatch, M, N, K, out):
+    """The CTA-pair block-scaled kernel (forced with BW_PAIR=1) against the oracle, including
+    M/N tails inside a 256 x 256 tile and K not a multiple of the 512-deep stage."""
+    import torch
+
+    monkeypatch.setenv("BW_PAIR", "1")
+    A = o.seeded_normal((M, K), 71)
+    B = o.seeded_normal((K, N), 72)
+    A[:, :5] *= 100.0  # a few blocks with large scales
+    qa, sfa = bwgemm.quantize_mxfp4(_t(A, cuda_dev), False, bwgemm.MX_BLOCK32)
+    qb, sfb = bwgemm.quantize_mxfp4(_t(B, cuda_dev), True, bwgemm.MX_BLOCK32)
+    C = _np(bwgemm.gemm_mxfp4(qa, qb, sfa, sfb, K, out_dtype=out))
+    torch.cuda.synchronize()
+    _status_ok()
+    ra, rsfa = o.quant_mxfp4(A, False, o.MX_BLOCK32)
+    rb, rsfb = o.quant_mxfp4(B, True, o.MX_BLOCK32)
+    da, db = o.dequant_mxfp4(ra, rsfa, K), o.dequant_mxfp4(rb, rsfb, K)
+    R = o.gemm_f64(da, db, b_trans=True)
+    tol = o.lowp_tolerance(K, np.abs(da).max(), np.abs(db).max(), np.abs(R).max(), out == bwgemm.OUT_BF16)
+    assert np.abs(C - R).max() <= tol
+
+
+@pytest.mark.parametrize("M,N,K", [(512, 512, 512), (300, 520, 1024)])
+def test_fp4_pair_kernel_parity(cuda_dev, monkeypatch, M, N, K):
+    import torch
+
+    monkeypatch.setenv("BW_PAIR", "1")
+    A = o.seeded_normal((M, K), 81)
+    B = o.seeded_normal((K, N), 82)
+    qa, sa = bwgemm.quantize_fp4(_t(A, cuda_dev), False, bwgemm.SCALE_AMAX, bwgemm.FP4_PACKED)
+    qb, sb = bwgemm.quantize_fp4(_t(B, cuda_dev), True, bwgemm.SCALE_AMAX, bwgemm.FP4_PACKED)
+    C = _np(bwgemm.gemm_fp4(qa, qb, K, sa, sb, out_dtype=bwgemm.OUT_F32))
+    torch.cuda.synchronize()
+    _status_ok()
+    ra, rsa = o.quant_fp4(A, False, o.SCALE_AMAX, o.FP4_PACKED)
+    rb, rsb = o.quant_fp4(B, True, o.SCALE_AMAX, o.FP4_PACKED)
+    da, db = o.dequant_mxfp4(ra, None, K), o.dequant_mxfp4(rb, None, K)
+    R = o.gemm_f64(da, db, b_trans=True) * np.float64(np.float32(rsa) * np.float32(rsb))
+    tol = o.lowp_tolerance(K, np.abs(da).max() * rsa, np.abs(db).max() * rsb)
+    assert np.abs(C - R).max() <= tol
