@@ -134,7 +134,7 @@ int launch_pair_mx(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorM
   const int tiles = ((p.M + 255) / 256) * ((p.N + 255) / 256);
   const int resident = max_clusters[dev & 63];
   const int clusters = tiles < resident ? tiles : resident;
-  p.trace = nullptr;
+  p.trace = trace_buffer(2 * clusters);  // word 0 (kernel cycles) only
   kern<<<2 * clusters, kMxThreads, MxPairCfg::kSmemBytes, stream>>>(ta, tb, tsa, tsb, p);
   BW_CUDA(cudaGetLastError());
   return BW_OK;

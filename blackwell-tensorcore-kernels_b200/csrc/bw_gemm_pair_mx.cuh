@@ -71,6 +71,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
   const int nk = (p.K + KE - 1) / KE;
   const bool unit_sf = p.sfa == nullptr;
   const WaitCtl wc{abort_flag, p.status, p.budget_ns};
+  const long long t_start = clock64();
+  const bool tracing = p.trace != nullptr;
+  unsigned long long tr_a = 0, tr_b = 0;
 
   // Scale-factor slots start at 2^0 (0x7f): the plain-FP4 path copies them once.
   for (int s = 0; s < kMxStages; ++s) {
@@ -114,7 +117,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
         const int arow = tm * TM + static_cast<int>(rank) * 128;
         const int bcol = tn * TN + static_cast<int>(rank) * 128;
         for (int kb = 0; kb < nk; ++kb) {
+          const long long w0 = tracing ? clock64() : 0;
           if (!mbar_wait(&empty[s], ph ^ 1, wc, 31)) { ok = false; break; }
+          if (tracing) tr_a += clock64() - w0;
           uint8_t* sA = smem + s * Cfg::kStageBytes;
           uint8_t* sB = sA + Cfg::kABytes;
           uint8_t* sSfa = sB + Cfg::kBBytes;
@@ -151,10 +156,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
       bool ok = true;
       bool sf_loaded = false;
       for (int t = cluster; t < num_tiles && ok; t += nclusters, ++local) {
+        const long long w1 = tracing ? clock64() : 0;
         if (!mbar_wait(accempty, (local & 1) ^ 1, wc, 32)) { ok = false; break; }
+        if (tracing) tr_b += clock64() - w1;
         tc_fence_after();
         for (int kb = 0; kb < nk; ++kb) {
+          const long long w2 = tracing ? clock64() : 0;
           if (!mbar_wait(&full[s], ph, wc, 33)) { ok = false; break; }
+          if (tracing) tr_a += clock64() - w2;
           tc_fence_after();
           const uint32_t aaddr = smem_u32(smem + s * Cfg::kStageBytes);
           const uint32_t baddr = aaddr + Cfg::kABytes;
@@ -207,7 +216,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
     for (int t = cluster; t < num_tiles; t += nclusters, ++local) {
       int tm, tn;
       tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
+      const long long w3 = tracing ? clock64() : 0;
       if (!mbar_wait(accfull, local & 1, wc, 35)) break;
+      const long long w4 = tracing ? clock64() : 0;
+      if (tracing) tr_a += w4 - w3;
       tc_fence_after();
       uint32_t r[128];
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + h * 128;
@@ -217,6 +229,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(accempty_leader);  // accumulator free: next tile may start
+      if (tracing) tr_b += clock64() - w4;  // drain time (TMEM -> registers)
       const int row = tm * TM + static_cast<int>(rank) * 128 + q * 32 + lane;
       if (row < p.M) {
         const int col0 = tn * TN + h * 128;
@@ -246,8 +259,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
     }
   }
 
+  if (tracing && lane == 0) {
+    unsigned long long* tr = p.trace + static_cast<size_t>(blockIdx.x) * kTraceWords;
+    if (warp == 0) tr[3] = tr_a;
+    if (warp == 1 && leader) { tr[1] = tr_a; tr[2] = tr_b; }
+    if (warp == 2) { tr[4] = tr_a; tr[5] = tr_b; }
+  }
   tc_fence_before();
   cluster_sync();
+  if (p.trace && threadIdx.x == 0) p.trace[static_cast<size_t>(blockIdx.x) * kTraceWords] = clock64() - t_start;
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
