@@ -40,6 +40,7 @@ for _p in (PKG, ORACLE):
 
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 DIM = 8192
+SHAPE = [DIM, DIM, DIM]  # M, N (per GPU), K; --shape overrides (e.g. the skinny 128x65536x8192)
 
 
 def load_peaks():
@@ -177,7 +178,7 @@ def timed_steps(step, K: int, W: int, world: int, stream):
     return max_over_ranks(ms, world)
 
 
-def make_inputs(workload: str, rank: int, dev):
+def make_inputs(workload: str, rank: int, dev):  # noqa: C901
     """Seeded synthetic inputs of the BASELINE shapes (per rank: its own column shard)."""
     import torch
 
@@ -186,7 +187,7 @@ def make_inputs(workload: str, rank: int, dev):
     ga.manual_seed(1234)
     gb = torch.Generator(device=dev)
     gb.manual_seed(4321 + 17 * rank)
-    M = N = K = DIM
+    M, N, K = SHAPE
     if workload == "f16":
         A = (torch.rand((M, K), generator=ga, device=dev) * 2 - 1).half()
         B = (torch.rand((K, N), generator=gb, device=dev) * 2 - 1).half()
@@ -230,7 +231,7 @@ def run_ours(args, world, rank, local):
     dev = torch.device("cuda", local)
     bwgemm.init(local)
     stream = torch.cuda.current_stream()
-    M = N = K = DIM
+    M, N, K = SHAPE
     flops = 2.0 * M * N * K
     clocks = ClockSampler(local)
     clocks.start()
@@ -346,7 +347,7 @@ def run_ours(args, world, rank, local):
         "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": dtype, "data": "synthetic (seeded uniform[-1,1] rounded to FP16)" if wl == "f16"
         else "synthetic (seeded N(0,1), quantised on device)",
-        "config": {"workload": f"{wl}_gemm_8192x8192x8192_per_gpu", "M": M, "N_per_gpu": N, "K": K,
+        "config": {"workload": f"{wl}_gemm_{M}x{N}x{K}_per_gpu", "M": M, "N_per_gpu": N, "K": K,
                    "N_total": N * world, "parallelism": f"column shards x{world} (no collective in the timed region)",
                    "l2": "inputs larger than L2 (A and B 8192x8192 each)",
                    "accumulate": "fp32", "out": "fp32" if wl == "f16" else "bf16"},
@@ -377,7 +378,7 @@ def compare_rows(args, wl, inp, dev, stream):
 
     import bwgemm
 
-    M = N = K = DIM
+    M, N, K = SHAPE
     flops = 2.0 * M * N * K
     out = {}
     block = max(10, min(args.steps, 50))
@@ -439,7 +440,7 @@ def run_reference(args, world, rank, local):
     dev = torch.device("cuda", local)
     # The reference's launchers run on the legacy default stream (src/main.cu:91-92).
     stream = torch.cuda.default_stream(dev)
-    M = N = K = DIM
+    M, N, K = SHAPE
     flops = 2.0 * M * N * K
     name = b"mma_warptile"
     inp = make_inputs("f16", rank, dev)
@@ -504,10 +505,14 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["f16", "fp8", "mxfp4", "fp4"], default="f16")
+    ap.add_argument("--shape", default=None, help="MxNxK per GPU (default 8192x8192x8192, BASELINE configs[1])")
     ap.add_argument("--gather", action="store_true", help="all-gather C over NCCL after timing (untimed)")
     ap.add_argument("--no-compare", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()
+    if args.shape:
+        SHAPE[:] = [int(x) for x in args.shape.lower().split("x")]
+        args.no_cpu = True  # the CPU baseline is defined on the headline workload
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

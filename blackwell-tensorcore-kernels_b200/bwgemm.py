@@ -67,6 +67,7 @@ def lib():
         "bw_device_status": [P, P],
         "bw_set_wait_budget_ns": [ctypes.c_ulonglong],
         "bw_set_trace_buffer": [P, I],
+        "bw_selftest_bounded_wait": [ctypes.c_ulonglong, P],
         "bw_gemm_f16": [P, P, P, I, I, I, P],
         "bw_gemm_f16_bt": [P, P, P, I, I, I, P],
         "bw_gemm_fp8": [P, P, P, P, P, I, I, I, I, P],

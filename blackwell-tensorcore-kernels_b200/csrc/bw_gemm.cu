@@ -172,6 +172,15 @@ int check_common(const void* A, const void* B, const void* C, int M, int N, int 
   return BW_OK;
 }
 
+// Skinny problems (one 128-row tile band, many columns) are HBM-bound streams of B: 128 x 64
+// tiles give enough tiles to balance 148 SMs and 8 stages keep ~190 KB of B in flight per SM.
+bool use_skinny(int M, int N, const DeviceState& d) {
+  // Measured slower than the CTA-pair kernel on 128 x 65536 x 8192 (259 vs 230 us): every 64-wide
+  // tile re-reads A from L2. Kept as an explicit option (BW_SKINNY=1) until split-K replaces it.
+  (void)M; (void)N; (void)d;
+  return env_int("BW_SKINNY", 0) != 0;
+}
+
 // Prefer 128 x 256 tiles; fall back to 128 x 128 when the wide tiles would leave SMs idle.
 bool use_narrow(int M, int N, const DeviceState& d) {
   const int forced = env_int("BW_TILE_N", 0);
@@ -189,9 +198,10 @@ int gemm_f16_impl(const void* A, const void* B, float* C, int M, int N, int K, c
   DeviceState* d;
   if ((r = ensure_device(&d)) != BW_OK) return r;
   if (K == 0) { BW_CUDA(cudaMemsetAsync(C, 0, sizeof(float) * size_t(M) * N, s)); return BW_OK; }
-  const bool pair = use_pair(M, N, *d);
-  const bool narrow = !pair && use_narrow(M, N, *d);
-  const int bn = pair ? 128 : narrow ? 128 : 256;
+  const bool skinny = use_skinny(M, N, *d);
+  const bool pair = !skinny && use_pair(M, N, *d);
+  const bool narrow = !pair && !skinny && use_narrow(M, N, *d);
+  const int bn = skinny ? 64 : pair ? 128 : narrow ? 128 : 256;
   CUtensorMap ta, tb;
   if ((r = make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, A, K, M, uint64_t(K) * 2, 64, 128)) != BW_OK) return r;
   if (b_mn) r = make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, B, N, K, uint64_t(N) * 2, 64, 64);
@@ -207,6 +217,10 @@ int gemm_f16_impl(const void* A, const void* B, float* C, int M, int N, int K, c
     }
     if (b_mn) return launch_pair<Kind::F16, true, 3, Out::F32, false, 2>(ta, tb, tc, p, s, *d);
     return launch_pair<Kind::F16, false, 3, Out::F32, false, 2>(ta, tb, tc, p, s, *d);
+  }
+  if (skinny) {
+    if (b_mn) return launch<Kind::F16, true, 64, 8, 2, Out::F32>(ta, tb, tc, p, s, *d);
+    return launch<Kind::F16, false, 64, 8, 2, Out::F32>(ta, tb, tc, p, s, *d);
   }
   if (b_mn) {
     if (narrow) return launch<Kind::F16, true, 128, 6, 2, Out::F32>(ta, tb, tc, p, s, *d);
@@ -228,9 +242,10 @@ int gemm_fp8_impl(const uint8_t* A, const uint8_t* Bt, const float* sa, const fl
   DeviceState* d;
   if ((r = ensure_device(&d)) != BW_OK) return r;
   if (K == 0) { BW_CUDA(cudaMemsetAsync(C, 0, out_elem_bytes(out_dtype) * size_t(M) * N, s)); return BW_OK; }
-  const bool pair = use_pair(M, N, *d);
-  const bool narrow = !pair && use_narrow(M, N, *d);
-  const int bn = pair ? 128 : narrow ? 128 : 256;
+  const bool skinny = use_skinny(M, N, *d);
+  const bool pair = !skinny && use_pair(M, N, *d);
+  const bool narrow = !pair && !skinny && use_narrow(M, N, *d);
+  const int bn = skinny ? 64 : pair ? 128 : narrow ? 128 : 256;
   CUtensorMap ta, tb;
   if ((r = make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, A, K, M, uint64_t(K), 128, 128)) != BW_OK) return r;
   if ((r = make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, Bt, K, N, uint64_t(K), 128, bn)) != BW_OK) return r;
@@ -247,6 +262,10 @@ int gemm_fp8_impl(const uint8_t* A, const uint8_t* Bt, const float* sa, const fl
     }
     if (direct) return launch_pair<Kind::F8, false, 3, Out::BF16, true, 2>(ta, tb, tc, p, s, *d);
     return launch_pair<Kind::F8, false, 3, Out::BF16, false, 2>(ta, tb, tc, p, s, *d);
+  }
+  if (skinny) {
+    if (out_dtype == BW_OUT_F32) return launch<Kind::F8, false, 64, 8, 2, Out::F32>(ta, tb, tc, p, s, *d);
+    return launch<Kind::F8, false, 64, 8, 2, Out::BF16>(ta, tb, tc, p, s, *d);
   }
   if (out_dtype == BW_OUT_F32) {
     if (narrow) return launch<Kind::F8, false, 128, 6, 2, Out::F32>(ta, tb, tc, p, s, *d);

@@ -18,7 +18,7 @@
 
 namespace bw {
 
-constexpr int kMxThreads = 320;  // producer, MMA, 8 epilogue warps
+constexpr int kMxThreads = 352;  // producer, MMA, 8 epilogue warps, scale-factor copier
 constexpr int kMxKsub = 2;
 constexpr int kMxStages = 3;
 
@@ -30,12 +30,14 @@ struct MxPairCfg {
   static constexpr int kSfbBytes = 2 * kSfaBytes;          // two 128-row blocks of B
   static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;
   static constexpr int kBarOffset = kMxStages * kStageBytes;
-  static constexpr int kNumBars = 2 * kMxStages + 2 + 1;  // full, empty, accfull, accempty, teardown
+  // full[S], empty[S], accfull, accempty, teardown, sf_ready[2], sf_free[2]
+  static constexpr int kNumBars = 2 * kMxStages + 3 + 4;
   static constexpr int kSmemBytes = kBarOffset + kNumBars * 8 + 16 + 1024;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
   static constexpr int kSfaCols = 4 * kMxKsub * 2;          // 4 atoms per stage x 4 columns
   static constexpr int kSfbCols = 2 * kSfaCols;             // two row blocks
-  static constexpr int kTmemCols = 512;                     // 256 accumulator + 48 SF, rounded up
+  static constexpr int kSfCols = kSfaCols + kSfbCols;       // 48 per buffer
+  static constexpr int kTmemCols = 512;                     // 256 accumulator + 2 x 48 SF, rounded up
 };
 
 template <Out OUT>
@@ -55,6 +57,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
   uint64_t* accfull = bars + 2 * kMxStages;
   uint64_t* accempty = accfull + 1;
   uint64_t* teardown = accfull + 2;
+  uint64_t* sf_ready = accfull + 3;  // [2]: scale factors of a stage are in TMEM buffer b
+  uint64_t* sf_free = accfull + 5;   // [2]: the MMAs reading TMEM buffer b have completed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -86,6 +90,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
     mbar_init(accfull, 1);
     mbar_init(accempty, 2 * 8);  // 8 epilogue warps in each CTA
     mbar_init(teardown, 1);
+    for (int b = 0; b < 2; ++b) { mbar_init(&sf_ready[b], 1); mbar_init(&sf_free[b], 1); }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -99,6 +104,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
   cluster_sync();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // scale-factor buffer b: SFA at 256 + 48b (16 columns), SFB right after (32 columns)
   const uint32_t tmem_sfa = tmem_base + 256;
   const uint32_t tmem_sfb = tmem_sfa + Cfg::kSfaCols;
 
@@ -155,6 +161,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
       int local = 0;
       bool ok = true;
       bool sf_loaded = false;
+      long long g = 0;  // stages consumed so far (all tiles)
       for (int t = cluster; t < num_tiles && ok; t += nclusters, ++local) {
         const long long w1 = tracing ? clock64() : 0;
         if (!mbar_wait(accempty, (local & 1) ^ 1, wc, 32)) { ok = false; break; }
@@ -169,16 +176,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
           const uint32_t baddr = aaddr + Cfg::kABytes;
           const uint32_t sfa_s = baddr + Cfg::kBBytes;
           const uint32_t sfb_s = sfa_s + Cfg::kSfaBytes;
-          if (!unit_sf || !sf_loaded) {
-            // SFA: 4 atoms -> columns [4a, 4a+4); SFB: atom a of row block rb -> 8a + 4rb.
+          uint32_t sfb_off = 0;  // column offset of the stage's scale-factor buffer
+          if (unit_sf) {
+            if (!sf_loaded) {  // plain FP4: the 0x7f slots of stage 0, copied once
 #pragma unroll
-            for (int a = 0; a < 4; ++a) {
-              tmem_cp_32x128b_warpx4_pair(tmem_sfa + 4 * a, sdesc_noswz(sfa_s + 512 * a, 16, 128));
-              tmem_cp_32x128b_warpx4_pair(tmem_sfb + 8 * a, sdesc_noswz(sfb_s + 512 * a, 16, 128));
-              tmem_cp_32x128b_warpx4_pair(tmem_sfb + 8 * a + 4,
-                                          sdesc_noswz(sfb_s + Cfg::kSfaBytes + 512 * a, 16, 128));
+              for (int a = 0; a < 4; ++a) {
+                tmem_cp_32x128b_warpx4_pair(tmem_sfa + 4 * a, sdesc_noswz(sfa_s + 512 * a, 16, 128));
+                tmem_cp_32x128b_warpx4_pair(tmem_sfb + 8 * a, sdesc_noswz(sfb_s + 512 * a, 16, 128));
+                tmem_cp_32x128b_warpx4_pair(tmem_sfb + 8 * a + 4,
+                                            sdesc_noswz(sfb_s + Cfg::kSfaBytes + 512 * a, 16, 128));
+              }
+              sf_loaded = true;
             }
-            sf_loaded = true;
+          } else {
+            // the copier warp has put this stage's scale factors into buffer (g & 1)
+            const int b = static_cast<int>(g & 1);
+            if (!mbar_wait(&sf_ready[b], static_cast<uint32_t>((g >> 1) & 1), wc, 36)) { ok = false; break; }
+            tc_fence_after();
+            sfb_off = b * Cfg::kSfCols;
           }
 #pragma unroll
           for (int kk = 0; kk < 4 * kMxKsub; ++kk) {
@@ -189,11 +204,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
             // MMA kk covers 64 K values = SF blocks 2kk, 2kk+1: atom kk/2, byte (2kk) % 4.
             const uint32_t sf_id = (2 * kk) & 3;
             const uint32_t atom = unit_sf ? 0u : static_cast<uint32_t>(kk >> 1);
-            umma_mxf4_pair(tmem_base, adesc, bdesc, idesc_mxf4(256, 256, sf_id, sf_id), tmem_sfa + 4 * atom,
-                           tmem_sfb + 8 * atom, acc);
+            umma_mxf4_pair(tmem_base, adesc, bdesc, idesc_mxf4(256, 256, sf_id, sf_id),
+                           tmem_sfa + sfb_off + 4 * atom, tmem_sfb + sfb_off + 8 * atom, acc);
           }
           umma_commit_pair(empty_own + s * 8);
           umma_commit_pair(empty_peer + s * 8);
+          if (!unit_sf) umma_commit_pair(smem_u32(&sf_free[g & 1]));
+          ++g;
           if (++s == kMxStages) { s = 0; ph ^= 1; }
         }
         if (ok) {
@@ -203,6 +220,37 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
       }
       umma_commit_pair(smem_u32(teardown));
       mbar_wait(teardown, 0, wc, 34);
+    }
+  } else if (warp == 10) {
+    // ---------------- scale-factor copier (leader only) ----------------
+    // Moves each stage's scale factors shared memory -> TMEM (both CTAs, cta_group::2) into
+    // one of two column buffers, so the MMA thread issues only MMAs and commits.
+    if (leader && lane == 0 && !unit_sf) {
+      int s = 0;
+      uint32_t ph = 0;
+      long long g = 0;
+      bool ok = true;
+      for (int t = cluster; t < num_tiles && ok; t += nclusters) {
+        for (int kb = 0; kb < nk; ++kb, ++g) {
+          const int b = static_cast<int>(g & 1);
+          const uint32_t u = static_cast<uint32_t>((g >> 1) & 1);
+          if (!mbar_wait(&full[s], ph, wc, 37)) { ok = false; break; }
+          if (!mbar_wait(&sf_free[b], u ^ 1, wc, 38)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sfa_s = smem_u32(smem + s * Cfg::kStageBytes) + Cfg::kABytes + Cfg::kBBytes;
+          const uint32_t sfb_s = sfa_s + Cfg::kSfaBytes;
+          const uint32_t off = b * Cfg::kSfCols;
+#pragma unroll
+          for (int a = 0; a < 4; ++a) {
+            tmem_cp_32x128b_warpx4_pair(tmem_sfa + off + 4 * a, sdesc_noswz(sfa_s + 512 * a, 16, 128));
+            tmem_cp_32x128b_warpx4_pair(tmem_sfb + off + 8 * a, sdesc_noswz(sfb_s + 512 * a, 16, 128));
+            tmem_cp_32x128b_warpx4_pair(tmem_sfb + off + 8 * a + 4,
+                                        sdesc_noswz(sfb_s + Cfg::kSfaBytes + 512 * a, 16, 128));
+          }
+          umma_commit_pair(smem_u32(&sf_ready[b]));
+          if (++s == kMxStages) { s = 0; ph ^= 1; }
+        }
+      }
     }
   } else {
     // ---------------- epilogue: warps 2..9, lane quarter q, column half h ----------------

@@ -8,9 +8,28 @@
 #include <cstdlib>
 #include <mutex>
 
+#include "bw_ptx.cuh"
 #include "bw_runtime.cuh"
 
 namespace bw {
+
+// Failure-detection self-test: one CTA waits on an mbarrier that nothing ever arrives at,
+// through the same bounded wait the GEMM kernels use. The wait must give up after the budget,
+// record the timeout in the device status word and return normally.
+__global__ void k_selftest_bounded_wait(int* status, unsigned long long budget_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const WaitCtl wc{&abort_flag, status, budget_ns};
+    mbar_wait(&bar, 0, wc, 99);
+  }
+}
 
 namespace {
 thread_local std::string g_err;
@@ -163,6 +182,17 @@ int bw_device_status(void* stream, int* out_status) {
   *out_status = v;
   if (v != 0) return set_error(BW_ERR_TIMEOUT, "kernel wait budget expired at site %d", v & 255);
   return BW_OK;
+}
+
+int bw_selftest_bounded_wait(unsigned long long budget_ns, void* stream) {
+  if (budget_ns == 0 || budget_ns > 10000000000ull) return set_error(BW_ERR_INVALID, "budget must be in (0, 10 s]");
+  DeviceState* d;
+  int r = ensure_device(&d);
+  if (r != BW_OK) return r;
+  k_selftest_bounded_wait<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(d->status, budget_ns);
+  BW_CUDA(cudaGetLastError());
+  int st = 0;
+  return bw_device_status(stream, &st);
 }
 
 int bw_set_trace_buffer(unsigned long long* dev_buf, int max_ctas) {

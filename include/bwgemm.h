@@ -75,6 +75,11 @@ int bw_device_status(void* stream, int* out_status);
  * waiting for free slabs, [4] epilogue cycles waiting for a finished accumulator,
  * [5] epilogue busy cycles, [6] tiles, [7] k-slabs. Diagnostic; no reference counterpart. */
 int bw_set_trace_buffer(unsigned long long* dev_buf, int max_ctas);
+/* Failure-detection self-test (no reference counterpart: the reference exits on errors).
+ * Launches one CTA that waits on an mbarrier nothing arrives at, through the same bounded
+ * wait as the GEMM kernels; returns BW_ERR_TIMEOUT after about budget_ns with the device
+ * status word cleared again, leaving the context usable. */
+int bw_selftest_bounded_wait(unsigned long long budget_ns, void* stream);
 /* Overrides the per-wait budget of every kernel (nanoseconds; default 2e9). */
 int bw_set_wait_budget_ns(unsigned long long ns);
 

@@ -326,3 +326,33 @@ def test_fp4_pair_kernel_parity(cuda_dev, monkeypatch, M, N, K):
     R = o.gemm_f64(da, db, b_trans=True) * np.float64(np.float32(rsa) * np.float32(rsb))
     tol = o.lowp_tolerance(K, np.abs(da).max() * rsa, np.abs(db).max() * rsb)
     assert np.abs(C - R).max() <= tol
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 4096, 1024), (77, 2056, 520), (1, 1024, 64)])
+@pytest.mark.parametrize("kind", ["f16", "fp8"])
+def test_skinny_kernel_parity(cuda_dev, monkeypatch, M, N, K, kind):
+    """The 128 x 64 single-CTA path for one-band (decode-style) shapes, forced with BW_SKINNY=1."""
+    import torch
+
+    monkeypatch.setenv("BW_SKINNY", "1")
+    if kind == "f16":
+        A = _f16(o.seeded_uniform((M, K), 91))
+        B = _f16(o.seeded_uniform((K, N), 92))
+        C = _np(bwgemm.gemm_f16(_t(A, cuda_dev).half(), _t(B, cuda_dev).half()))
+        R = o.gemm_f64(A, B)
+        tol = o.f16_tolerance(K, np.abs(A).max(), np.abs(B).max())
+    else:
+        if K % 16:
+            pytest.skip("fp8 needs K % 16 == 0")
+        A = o.seeded_normal((M, K), 93)
+        B = o.seeded_normal((K, N), 94)
+        qa, sa = bwgemm.quantize_fp8(_t(A, cuda_dev), False, bwgemm.SCALE_AMAX)
+        qb, sb = bwgemm.quantize_fp8(_t(B, cuda_dev), True, bwgemm.SCALE_AMAX)
+        C = _np(bwgemm.gemm_fp8(qa, qb, sa, sb, out_dtype=bwgemm.OUT_F32))
+        ra, rsa = o.quant_fp8(A, False, o.SCALE_AMAX)
+        rb, rsb = o.quant_fp8(B, True, o.SCALE_AMAX)
+        R = o.gemm_f64(o.dequant_fp8(ra), o.dequant_fp8(rb), b_trans=True) * float(np.float32(rsa) * np.float32(rsb))
+        tol = o.lowp_tolerance(K, 448 * rsa, 448 * rsb)
+    torch.cuda.synchronize()
+    _status_ok()
+    assert np.abs(C - R).max() <= tol
