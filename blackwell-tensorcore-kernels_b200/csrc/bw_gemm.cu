@@ -38,11 +38,11 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, 
   return BW_OK;
 }
 
-template <Kind KIND, bool B_MN, int STAGES, Out OUT, bool DIRECT_EPI, int KSUB>
+template <Kind KIND, bool B_MN, int STAGES, Out OUT, bool DIRECT_EPI, int KSUB, int TN = 256>
 int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, GemmParams p,
                 cudaStream_t stream, const DeviceState& d) {
-  using Cfg = PairCfg<KIND, STAGES, DIRECT_EPI, KSUB>;
-  auto kern = bw_tc_gemm_pair_kernel<KIND, B_MN, STAGES, OUT, DIRECT_EPI, KSUB>;
+  using Cfg = PairCfg<KIND, STAGES, DIRECT_EPI, KSUB, TN>;
+  auto kern = bw_tc_gemm_pair_kernel<KIND, B_MN, STAGES, OUT, DIRECT_EPI, KSUB, TN>;
   static bool attr_done[64] = {};
   int dev = 0;
   BW_CUDA(cudaGetDevice(&dev));
@@ -72,7 +72,7 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
     }
     max_clusters[dev & 63] = n;
   }
-  const int tiles = ((p.M + 255) / 256) * ((p.N + 255) / 256);
+  const int tiles = ((p.M + 255) / 256) * ((p.N + TN - 1) / TN);
   const int resident = max_clusters[dev & 63];
   int clusters = tiles < resident ? tiles : resident;
   const int cap = env_int("BW_MAX_CTAS", 0);
@@ -88,9 +88,11 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
 // per clock versus 75% with one atom per stage. The epilogue stores 32-byte sectors straight
 // from registers when C is 32-byte aligned (no staging shared memory), else stages through
 // shared memory and TMA stores.
-bool direct_epilogue_ok(const void* C) {
+// Every 256-bit store must start on a 32-byte boundary: the base of C and every row pitch
+// (N * element bytes) must be multiples of 32 (BF16 output therefore needs N % 16 == 0).
+bool direct_epilogue_ok(const void* C, int N, int elem_bytes) {
   if (env_int("BW_EPI_DIRECT", 1) == 0) return false;
-  return (reinterpret_cast<uintptr_t>(C) & 31u) == 0;
+  return (reinterpret_cast<uintptr_t>(C) & 31u) == 0 && (static_cast<long long>(N) * elem_bytes) % 32 == 0;
 }
 
 // CTA pairs (256 x 256 tiles) when the problem fills at least most of the SM pairs.
@@ -211,7 +213,7 @@ int gemm_f16_impl(const void* A, const void* B, float* C, int M, int N, int K, c
   if ((r = make_c_map(&tc, C, M, N, BW_OUT_F32)) != BW_OK) return r;
   GemmParams p = base_params(*d, C, M, N, K);
   if (pair) {
-    if (direct_epilogue_ok(C)) {
+    if (direct_epilogue_ok(C, N, 4)) {
       if (b_mn) return launch_pair<Kind::F16, true, 3, Out::F32, true, 2>(ta, tb, tc, p, s, *d);
       return launch_pair<Kind::F16, false, 3, Out::F32, true, 2>(ta, tb, tc, p, s, *d);
     }
@@ -255,7 +257,7 @@ int gemm_fp8_impl(const uint8_t* A, const uint8_t* Bt, const float* sa, const fl
   p.scale_a = sa;
   p.scale_b = sb;
   if (pair) {
-    const bool direct = direct_epilogue_ok(C);
+    const bool direct = direct_epilogue_ok(C, N, static_cast<int>(out_elem_bytes(out_dtype)));
     if (out_dtype == BW_OUT_F32) {
       if (direct) return launch_pair<Kind::F8, false, 3, Out::F32, true, 2>(ta, tb, tc, p, s, *d);
       return launch_pair<Kind::F8, false, 3, Out::F32, false, 2>(ta, tb, tc, p, s, *d);
@@ -301,6 +303,15 @@ int gemm_mxf4_impl(const uint8_t* A, const uint8_t* Bt, const uint8_t* sfa, cons
   p.sf_kgroups = ((K + 31) / 32 + 3) / 4;
   const bool pair_ok = env_int("BW_MX_PAIR", 1) != 0 && use_pair(M, N, *d) &&
                        (out_dtype == BW_OUT_BF16 || (reinterpret_cast<uintptr_t>(C) & 31u) == 0);
+  if (pair_ok && unit_sf && direct_epilogue_ok(C, N, static_cast<int>(out_elem_bytes(out_dtype))) && env_int("BW_FP4_TN224", 1) != 0) {
+    // plain FP4: constant 2^0 block scales need only 12 TMEM columns, which leaves room for two
+    // 224-column accumulators - the double-buffered pair kernel with 256 x 224 tiles
+    CUtensorMap ta2, tb2;
+    if ((r = make_tmap_2d(&ta2, CU_TENSOR_MAP_DATA_TYPE_UINT8, A, K / 2, M, uint64_t(K / 2), 128, 128)) != BW_OK) return r;
+    if ((r = make_tmap_2d(&tb2, CU_TENSOR_MAP_DATA_TYPE_UINT8, Bt, K / 2, N, uint64_t(K / 2), 128, 112)) != BW_OK) return r;
+    if (out_dtype == BW_OUT_F32) return launch_pair<Kind::MXF4, false, 3, Out::F32, true, 2, 224>(ta2, tb2, tc, p, s, *d);
+    return launch_pair<Kind::MXF4, false, 3, Out::BF16, true, 2, 224>(ta2, tb2, tc, p, s, *d);
+  }
   if (pair_ok) {
     CUtensorMap ta2, tb2, tsa, tsb;
     if ((r = make_tmap_2d(&ta2, CU_TENSOR_MAP_DATA_TYPE_UINT8, A, K / 2, M, uint64_t(K / 2), 128, 128)) != BW_OK) return r;

@@ -127,6 +127,7 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
 template <Out OUT, int NCOLS, typename Release>
 __device__ __forceinline__ void epilogue_tile_direct(uint32_t tbase, const GemmParams& p, int row, int col0,
                                                      float alpha, Release release) {
+  static_assert(NCOLS % 32 == 0, "tile width must be whole 32-column chunks");
 #pragma unroll 1
   for (int c = 0; c < NCOLS; c += 32) {
     uint32_t r[32];
@@ -172,6 +173,7 @@ __device__ __forceinline__ void epilogue_tile(uint32_t tbase, const CUtensorMap*
                                               uint8_t* wbuf, int& uses, int lane, uint64_t store_policy,
                                               bool hinted, Release release) {
   constexpr int kCols = (OUT == Out::F32) ? 32 : 64;  // columns per 128-byte row chunk
+  static_assert(NCOLS % kCols == 0, "tile width must be whole 128-byte chunks");
   const uint32_t row_addr = smem_u32(wbuf) + lane * 128;
 #pragma unroll 1
   for (int c = 0; c < NCOLS; c += kCols) {

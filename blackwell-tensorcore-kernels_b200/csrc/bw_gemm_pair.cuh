@@ -20,28 +20,34 @@
 
 namespace bw {
 
-template <Kind KIND, int STAGES, bool DIRECT_EPI = false, int KSUB = 1>
+template <Kind KIND, int STAGES, bool DIRECT_EPI = false, int KSUB = 1, int TN = 256>
 struct PairCfg {
   static constexpr int kAtomBytes = 128 * kSlabBytes;  // 128 rows x one 128-byte swizzle atom of K
+  static constexpr int kBAtomBytes = (TN / 2) * kSlabBytes;
   static constexpr int kABytes = KSUB * kAtomBytes;    // this CTA's 128 rows of A, KSUB atoms of K
-  static constexpr int kBBytes = KSUB * kAtomBytes;    // this CTA's 128 columns of B
+  static constexpr int kBBytes = KSUB * kBAtomBytes;   // this CTA's TN/2 columns of B
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kEpiOffset = STAGES * kStageBytes;
-  static constexpr int kBarOffset = kEpiOffset + (DIRECT_EPI ? 0 : kEpiBytes);
+  // plain FP4 (kind::mxf4 with every block scale 2^0): 3 constant scale-factor atoms
+  static constexpr int kSfOffset = kEpiOffset + (DIRECT_EPI ? 0 : kEpiBytes);
+  static constexpr int kSfBytes = (KIND == Kind::MXF4) ? 3 * 512 : 0;
+  static constexpr int kBarOffset = kSfOffset + kSfBytes;
+  static_assert(TN % 32 == 0 && TN <= 256 && (KIND == Kind::MXF4 ? 2 * TN + 12 <= 512 : TN == 256), "tile N");
   static constexpr int kNumBars = 2 * STAGES + 2 * 2 + 1;
   static constexpr int kSmemBytes = kBarOffset + kNumBars * 8 + 16 + 1024;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
   static constexpr int kTmemCols = 512;  // two 256-column FP32 accumulators
 };
 
-template <Kind KIND, bool B_MN, int STAGES, Out OUT, bool DIRECT_EPI, int KSUB>
+template <Kind KIND, bool B_MN, int STAGES, Out OUT, bool DIRECT_EPI, int KSUB, int TN = 256>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     bw_tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                            const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
-  using Cfg = PairCfg<KIND, STAGES, DIRECT_EPI, KSUB>;
+  using Cfg = PairCfg<KIND, STAGES, DIRECT_EPI, KSUB, TN>;
+  static_assert(!B_MN || TN == 256, "N-major B is loaded as 64-column boxes of a 256-wide tile");
   constexpr int KX = KindTraits<KIND>::kCoordPerSlab;          // tensor-map units per swizzle atom
   constexpr int KE = KindTraits<KIND>::kElemsPerSlab * KSUB;   // K elements per pipeline stage
-  constexpr int TM = 256, TN = 256;
+  constexpr int TM = 256;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kBarOffset);
@@ -69,6 +75,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const long long t_start = clock64();
   unsigned long long tr_a = 0, tr_b = 0, tr_c = 0;  // role-specific wait counters
 
+  if constexpr (KIND == Kind::MXF4) {
+    uint32_t* sf = reinterpret_cast<uint32_t*>(smem + Cfg::kSfOffset);
+    for (int i = threadIdx.x; i < Cfg::kSfBytes / 4; i += kThreads) sf[i] = 0x7f7f7f7fu;  // 2^0
+    fence_proxy_async_smem();
+  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
     for (int b = 0; b < 2; ++b) { mbar_init(&accfull[b], 1); mbar_init(&accempty[b], 2 * kEpiWarps); }
@@ -95,7 +106,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         int tm, tn;
         tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
         const int arow = tm * TM + static_cast<int>(rank) * 128;
-        const int bcol = tn * TN + static_cast<int>(rank) * 128;
+        const int bcol = tn * TN + static_cast<int>(rank) * (TN / 2);
         for (int kb = 0; kb < nk; ++kb) {
           const long long w0 = tracing ? clock64() : 0;
           if (!mbar_wait(&empty[s], ph ^ 1, wc, 11)) { ok = false; break; }
@@ -112,7 +123,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
               tma_load_2d_pair(&tmB, fb, sB + j * Cfg::kAtomBytes, bcol, ka * 64, pol);
               tma_load_2d_pair(&tmB, fb, sB + j * Cfg::kAtomBytes + 64 * kSlabBytes, bcol + 64, ka * 64, pol);
             } else {
-              tma_load_2d_pair(&tmB, fb, sB + j * Cfg::kAtomBytes, ka * KX, bcol, pol);
+              tma_load_2d_pair(&tmB, fb, sB + j * Cfg::kBAtomBytes, ka * KX, bcol, pol);
             }
           }
           if (++s == STAGES) { s = 0; ph ^= 1; }
@@ -122,7 +133,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer (leader CTA only) ----------------
     if (leader && lane == 0) {
-      const uint32_t idesc = idesc_dense(KindTraits<KIND>::kFmt, KindTraits<KIND>::kFmt, B_MN, 256, 256);
+      const uint32_t idesc = (KIND == Kind::MXF4) ? 0u
+                             : idesc_dense(KindTraits<KIND>::kFmt, KindTraits<KIND>::kFmt, B_MN, 256, TN);
+      const uint32_t tmem_sf = tmem_base + 2 * TN;  // plain FP4: SFA atom at +0, SFB blocks at +4, +8
+      if constexpr (KIND == Kind::MXF4) {
+        const uint32_t sf_s = smem_u32(smem + Cfg::kSfOffset);
+#pragma unroll
+        for (int a = 0; a < 3; ++a) tmem_cp_32x128b_warpx4_pair(tmem_sf + 4 * a, sdesc_noswz(sf_s + 512 * a, 16, 128));
+      }
       const uint32_t empty_own = smem_u32(empty), empty_peer = mapa_shared(smem_u32(empty), peer);
       const uint32_t accfull_own = smem_u32(accfull), accfull_peer = mapa_shared(smem_u32(accfull), peer);
       int s = 0;
@@ -136,7 +154,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (!mbar_wait(&accempty[b], aph ^ 1, wc, 12)) { ok = false; break; }
         if (tracing) tr_b += clock64() - w1;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + b * 256;
+        const uint32_t d_tmem = tmem_base + b * TN;
         for (int kb = 0; kb < nk; ++kb) {
           const long long w2 = tracing ? clock64() : 0;
           if (!mbar_wait(&full[s], ph, wc, 13)) { ok = false; break; }
@@ -152,9 +170,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             uint64_t bdesc;
             if constexpr (B_MN)
               bdesc = sdesc_sw128(baddr + j * Cfg::kAtomBytes + k * 16 * kSlabBytes, 64 * kSlabBytes, 1024);
-            else bdesc = sdesc_sw128(baddr + j * Cfg::kAtomBytes + k * 32, 16, 1024);
+            else bdesc = sdesc_sw128(baddr + j * Cfg::kBAtomBytes + k * 32, 16, 1024);
             if constexpr (KIND == Kind::F16) umma_f16_pair(d_tmem, adesc, bdesc, idesc, acc);
-            else umma_f8f6f4_pair(d_tmem, adesc, bdesc, idesc, acc);
+            else if constexpr (KIND == Kind::F8) umma_f8f6f4_pair(d_tmem, adesc, bdesc, idesc, acc);
+            else umma_mxf4_pair(d_tmem, adesc, bdesc, idesc_mxf4(256, TN, (2 * k) & 3, (2 * k) & 3), tmem_sf,
+                                tmem_sf + 4, acc);
           }
           umma_commit_pair(empty_own + s * 8);
           umma_commit_pair(empty_peer + s * 8);
@@ -189,7 +209,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const long long w4 = tracing ? clock64() : 0;
       if (tracing) tr_a += w4 - w3;
       tc_fence_after();
-      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * 256;
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * TN;
       auto release = [&] {
         tc_fence_before();
         __syncwarp();

@@ -308,8 +308,9 @@ def test_mxfp4_pair_kernel_parity(cuda_dev, monkeypatch, M, N, K, out):
     assert np.abs(C - R).max() <= tol
 
 
-@pytest.mark.parametrize("M,N,K", [(512, 512, 512), (300, 520, 1024)])
-def test_fp4_pair_kernel_parity(cuda_dev, monkeypatch, M, N, K):
+@pytest.mark.parametrize("M,N,K", [(512, 512, 512), (300, 520, 1024), (1024, 2240, 2048)])
+@pytest.mark.parametrize("out", [bwgemm.OUT_F32, bwgemm.OUT_BF16])
+def test_fp4_pair_kernel_parity(cuda_dev, monkeypatch, M, N, K, out):
     import torch
 
     monkeypatch.setenv("BW_PAIR", "1")
@@ -317,14 +318,15 @@ def test_fp4_pair_kernel_parity(cuda_dev, monkeypatch, M, N, K):
     B = o.seeded_normal((K, N), 82)
     qa, sa = bwgemm.quantize_fp4(_t(A, cuda_dev), False, bwgemm.SCALE_AMAX, bwgemm.FP4_PACKED)
     qb, sb = bwgemm.quantize_fp4(_t(B, cuda_dev), True, bwgemm.SCALE_AMAX, bwgemm.FP4_PACKED)
-    C = _np(bwgemm.gemm_fp4(qa, qb, K, sa, sb, out_dtype=bwgemm.OUT_F32))
+    C = _np(bwgemm.gemm_fp4(qa, qb, K, sa, sb, out_dtype=out))
     torch.cuda.synchronize()
     _status_ok()
     ra, rsa = o.quant_fp4(A, False, o.SCALE_AMAX, o.FP4_PACKED)
     rb, rsb = o.quant_fp4(B, True, o.SCALE_AMAX, o.FP4_PACKED)
     da, db = o.dequant_mxfp4(ra, None, K), o.dequant_mxfp4(rb, None, K)
     R = o.gemm_f64(da, db, b_trans=True) * np.float64(np.float32(rsa) * np.float32(rsb))
-    tol = o.lowp_tolerance(K, np.abs(da).max() * rsa, np.abs(db).max() * rsb)
+    tol = o.lowp_tolerance(K, np.abs(da).max() * rsa, np.abs(db).max() * rsb, np.abs(R).max(),
+                           out == bwgemm.OUT_BF16)
     assert np.abs(C - R).max() <= tol
 
 
@@ -355,4 +357,26 @@ def test_skinny_kernel_parity(cuda_dev, monkeypatch, M, N, K, kind):
         tol = o.lowp_tolerance(K, 448 * rsa, 448 * rsb)
     torch.cuda.synchronize()
     _status_ok()
+    assert np.abs(C - R).max() <= tol
+
+
+@pytest.mark.parametrize("N", [520, 1032])
+def test_fp8_pair_bf16_out_with_unaligned_row_pitch(cuda_dev, monkeypatch, N):
+    """N % 16 == 8 makes BF16 rows 16- but not 32-byte aligned: the pair kernel must take the
+    staged epilogue, not the 32-byte direct stores."""
+    import torch
+
+    monkeypatch.setenv("BW_PAIR", "1")
+    M, K = 512, 512
+    A = o.seeded_normal((M, K), 101)
+    B = o.seeded_normal((K, N), 102)
+    qa, sa = bwgemm.quantize_fp8(_t(A, cuda_dev), False, bwgemm.SCALE_AMAX)
+    qb, sb = bwgemm.quantize_fp8(_t(B, cuda_dev), True, bwgemm.SCALE_AMAX)
+    C = _np(bwgemm.gemm_fp8(qa, qb, sa, sb, out_dtype=bwgemm.OUT_BF16))
+    torch.cuda.synchronize()
+    _status_ok()
+    ra, rsa = o.quant_fp8(A, False, o.SCALE_AMAX)
+    rb, rsb = o.quant_fp8(B, True, o.SCALE_AMAX)
+    R = o.gemm_f64(o.dequant_fp8(ra), o.dequant_fp8(rb), b_trans=True) * float(np.float32(rsa) * np.float32(rsb))
+    tol = o.lowp_tolerance(K, 448 * rsa, 448 * rsb, np.abs(R).max(), True)
     assert np.abs(C - R).max() <= tol
