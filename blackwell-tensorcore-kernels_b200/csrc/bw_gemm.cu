@@ -104,21 +104,22 @@ bool use_pair(int M, int N, const DeviceState& d) {
   return tiles >= d.sms / 2;
 }
 
-template <Out OUT>
+template <Out OUT, int TN>
 int launch_pair_mx(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tsa, const CUtensorMap& tsb,
                    GemmParams p, cudaStream_t stream, const DeviceState& d) {
-  auto kern = bw_tc_gemm_pair_mx_kernel<OUT>;
+  using Cfg = MxPairCfg<TN>;
+  auto kern = bw_tc_gemm_pair_mx_kernel<OUT, TN>;
   static bool attr_done[64] = {};
   static int max_clusters[64] = {};
   int dev = 0;
   BW_CUDA(cudaGetDevice(&dev));
   if (!attr_done[dev & 63]) {
-    BW_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, MxPairCfg::kSmemBytes));
+    BW_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
     attr_done[dev & 63] = true;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * (d.sms / 2), 1, 1);
     cfg.blockDim = dim3(kMxThreads, 1, 1);
-    cfg.dynamicSmemBytes = MxPairCfg::kSmemBytes;
+    cfg.dynamicSmemBytes = Cfg::kSmemBytes;
     cudaLaunchAttribute attr;
     attr.id = cudaLaunchAttributeClusterDimension;
     attr.val.clusterDim.x = 2;
@@ -133,11 +134,11 @@ int launch_pair_mx(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorM
     }
     max_clusters[dev & 63] = n;
   }
-  const int tiles = ((p.M + 255) / 256) * ((p.N + 255) / 256);
+  const int tiles = ((p.M + 255) / 256) * ((p.N + TN - 1) / TN);
   const int resident = max_clusters[dev & 63];
   const int clusters = tiles < resident ? tiles : resident;
   p.trace = trace_buffer(2 * clusters);  // word 0 (kernel cycles) only
-  kern<<<2 * clusters, kMxThreads, MxPairCfg::kSmemBytes, stream>>>(ta, tb, tsa, tsb, p);
+  kern<<<2 * clusters, kMxThreads, Cfg::kSmemBytes, stream>>>(ta, tb, tsa, tsb, p);
   BW_CUDA(cudaGetLastError());
   return BW_OK;
 }
@@ -313,9 +314,14 @@ int gemm_mxf4_impl(const uint8_t* A, const uint8_t* Bt, const uint8_t* sfa, cons
     return launch_pair<Kind::MXF4, false, 3, Out::BF16, true, 2, 224>(ta2, tb2, tc, p, s, *d);
   }
   if (pair_ok) {
+    // 256 x 192 tiles (two accumulators, direct 32-byte stores) when C allows them, else
+    // 256 x 256 with one accumulator drained to registers
+    const bool narrow_mx = direct_epilogue_ok(C, N, static_cast<int>(out_elem_bytes(out_dtype))) &&
+                           env_int("BW_MX_TN", 256) == 192;
     CUtensorMap ta2, tb2, tsa, tsb;
     if ((r = make_tmap_2d(&ta2, CU_TENSOR_MAP_DATA_TYPE_UINT8, A, K / 2, M, uint64_t(K / 2), 128, 128)) != BW_OK) return r;
-    if ((r = make_tmap_2d(&tb2, CU_TENSOR_MAP_DATA_TYPE_UINT8, Bt, K / 2, N, uint64_t(K / 2), 128, 128)) != BW_OK) return r;
+    if ((r = make_tmap_2d(&tb2, CU_TENSOR_MAP_DATA_TYPE_UINT8, Bt, K / 2, N, uint64_t(K / 2), 128,
+                          narrow_mx ? 96 : 128)) != BW_OK) return r;
     if (sfa) {
       // scale factors seen as rows of 256 bytes; one box = 8 rows = 4 atoms of 512 B
       const uint64_t ra = bw_sf_bytes(M, K) / 256, rb = bw_sf_bytes(N, K) / 256;
@@ -327,8 +333,12 @@ int gemm_mxf4_impl(const uint8_t* A, const uint8_t* Bt, const uint8_t* sfa, cons
       tsa = ta2;  // unused: plain FP4 keeps every block scale at 2^0
       tsb = tb2;
     }
-    if (out_dtype == BW_OUT_F32) return launch_pair_mx<Out::F32>(ta2, tb2, tsa, tsb, p, s, *d);
-    return launch_pair_mx<Out::BF16>(ta2, tb2, tsa, tsb, p, s, *d);
+    if (narrow_mx) {
+      if (out_dtype == BW_OUT_F32) return launch_pair_mx<Out::F32, 192>(ta2, tb2, tsa, tsb, p, s, *d);
+      return launch_pair_mx<Out::BF16, 192>(ta2, tb2, tsa, tsb, p, s, *d);
+    }
+    if (out_dtype == BW_OUT_F32) return launch_pair_mx<Out::F32, 256>(ta2, tb2, tsa, tsb, p, s, *d);
+    return launch_pair_mx<Out::BF16, 256>(ta2, tb2, tsa, tsb, p, s, *d);
   }
   if (out_dtype == BW_OUT_F32) return launch<Kind::MXF4, false, 128, 5, 2, Out::F32>(ta, tb, tc, p, s, *d);
   return launch<Kind::MXF4, false, 128, 5, 2, Out::BF16>(ta, tb, tc, p, s, *d);

@@ -22,43 +22,53 @@ constexpr int kMxThreads = 352;  // producer, MMA, 8 epilogue warps, scale-facto
 constexpr int kMxKsub = 2;
 constexpr int kMxStages = 3;
 
+// TN = 256: one 256-column accumulator, 8 epilogue warps drain it to registers.
+// TN = 192: two 192-column accumulators (epilogue overlaps the next tile), 4 epilogue warps
+//           with direct stores; a tile's B rows start at offset 0 or 64 inside a 128-row
+//           scale-factor block, which shifts the SFB TMEM address by 0 or 2 columns.
+template <int TN>
 struct MxPairCfg {
+  static_assert(TN == 192 || TN == 256, "block-scaled tile N");
+  static constexpr int kAccBufs = TN == 192 ? 2 : 1;
   static constexpr int kAtom = 128 * kSlabBytes;           // 128 rows x 128 B
+  static constexpr int kBAtom = (TN / 2) * kSlabBytes;     // this CTA's TN/2 rows of Bt
   static constexpr int kABytes = kMxKsub * kAtom;          // 32 KB
-  static constexpr int kBBytes = kMxKsub * kAtom;          // 32 KB
+  static constexpr int kBBytes = kMxKsub * kBAtom;         // 32 or 24 KB
   static constexpr int kSfaBytes = kMxKsub * 1024;         // 2 SF atoms (512 B) per K atom of 256
   static constexpr int kSfbBytes = 2 * kSfaBytes;          // two 128-row blocks of B
   static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;
   static constexpr int kBarOffset = kMxStages * kStageBytes;
-  // full[S], empty[S], accfull, accempty, teardown, sf_ready[2], sf_free[2]
-  static constexpr int kNumBars = 2 * kMxStages + 3 + 4;
+  // full[S], empty[S], accfull[2], accempty[2], teardown, sf_ready[2], sf_free[2]
+  static constexpr int kNumBars = 2 * kMxStages + 5 + 4;
   static constexpr int kSmemBytes = kBarOffset + kNumBars * 8 + 16 + 1024;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
   static constexpr int kSfaCols = 4 * kMxKsub * 2;          // 4 atoms per stage x 4 columns
   static constexpr int kSfbCols = 2 * kSfaCols;             // two row blocks
   static constexpr int kSfCols = kSfaCols + kSfbCols;       // 48 per buffer
-  static constexpr int kTmemCols = 512;                     // 256 accumulator + 2 x 48 SF, rounded up
+  static constexpr int kSfBase = kAccBufs * TN;            // first scale-factor column
+  static constexpr int kTmemCols = 512;
+  static_assert(kSfBase + 2 * kSfCols <= kTmemCols, "TMEM budget");
 };
 
-template <Out OUT>
+template <Out OUT, int TN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
     bw_tc_gemm_pair_mx_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                               const __grid_constant__ CUtensorMap tmSfa, const __grid_constant__ CUtensorMap tmSfb,
                               const GemmParams p) {
-  using Cfg = MxPairCfg;
+  using Cfg = MxPairCfg<TN>;
   constexpr int KX = 128;    // packed bytes per K atom (256 FP4 values)
   constexpr int KE = 256 * kMxKsub;
-  constexpr int TM = 256, TN = 256;
+  constexpr int TM = 256;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kBarOffset);
   uint64_t* full = bars;
   uint64_t* empty = bars + kMxStages;
   uint64_t* accfull = bars + 2 * kMxStages;
-  uint64_t* accempty = accfull + 1;
-  uint64_t* teardown = accfull + 2;
-  uint64_t* sf_ready = accfull + 3;  // [2]: scale factors of a stage are in TMEM buffer b
-  uint64_t* sf_free = accfull + 5;   // [2]: the MMAs reading TMEM buffer b have completed
+  uint64_t* accempty = accfull + 2;
+  uint64_t* teardown = accfull + 4;
+  uint64_t* sf_ready = accfull + 5;  // [2]: scale factors of a stage are in TMEM buffer b
+  uint64_t* sf_free = accfull + 7;   // [2]: the MMAs reading TMEM buffer b have completed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -87,8 +97,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
   fence_proxy_async_smem();
   if (threadIdx.x == 0) {
     for (int s = 0; s < kMxStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-    mbar_init(accfull, 1);
-    mbar_init(accempty, 2 * 8);  // 8 epilogue warps in each CTA
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accfull[b], 1);
+      mbar_init(&accempty[b], 2 * (TN == 192 ? 4 : 8));  // epilogue warps of both CTAs
+    }
     mbar_init(teardown, 1);
     for (int b = 0; b < 2; ++b) { mbar_init(&sf_ready[b], 1); mbar_init(&sf_free[b], 1); }
     *abort_flag = 0;
@@ -105,7 +117,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   // scale-factor buffer b: SFA at 256 + 48b (16 columns), SFB right after (32 columns)
-  const uint32_t tmem_sfa = tmem_base + 256;
+  const uint32_t tmem_sfa = tmem_base + Cfg::kSfBase;
   const uint32_t tmem_sfb = tmem_sfa + Cfg::kSfaCols;
 
   if (warp == 0) {
@@ -121,7 +133,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
         int tm, tn;
         tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
         const int arow = tm * TM + static_cast<int>(rank) * 128;
-        const int bcol = tn * TN + static_cast<int>(rank) * 128;
+        const int bcol = tn * TN + static_cast<int>(rank) * (TN / 2);
+        const int sfb_block = (tn * TN) / 128;  // first 128-row SF block the tile's B rows touch
         for (int kb = 0; kb < nk; ++kb) {
           const long long w0 = tracing ? clock64() : 0;
           if (!mbar_wait(&empty[s], ph ^ 1, wc, 31)) { ok = false; break; }
@@ -136,7 +149,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
           for (int j = 0; j < kMxKsub; ++j) {
             const int ka = kb * kMxKsub + j;
             tma_load_2d_pair(&tmA, fb, sA + j * Cfg::kAtom, ka * KX, arow, pol);
-            tma_load_2d_pair(&tmB, fb, sB + j * Cfg::kAtom, ka * KX, bcol, pol);
+            tma_load_2d_pair(&tmB, fb, sB + j * Cfg::kBAtom, ka * KX, bcol, pol);
           }
           if (!unit_sf) {
             // SF buffers viewed as rows of 256 B (an atom = 2 rows); a stage needs 4 atoms
@@ -144,8 +157,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
             // row block read the next block's scales for zero-filled K, past the buffer zeros.
             const int kg0 = kb * 4;
             tma_load_2d_pair(&tmSfa, fb, sSfa, 0, ((tm * 2 + static_cast<int>(rank)) * p.sf_kgroups + kg0) * 2, pol);
-            tma_load_2d_pair(&tmSfb, fb, sSfb, 0, ((tn * 2) * p.sf_kgroups + kg0) * 2, pol);
-            tma_load_2d_pair(&tmSfb, fb, sSfb + Cfg::kSfaBytes, 0, ((tn * 2 + 1) * p.sf_kgroups + kg0) * 2, pol);
+            tma_load_2d_pair(&tmSfb, fb, sSfb, 0, (sfb_block * p.sf_kgroups + kg0) * 2, pol);
+            tma_load_2d_pair(&tmSfb, fb, sSfb + Cfg::kSfaBytes, 0, ((sfb_block + 1) * p.sf_kgroups + kg0) * 2, pol);
           }
           if (++s == kMxStages) { s = 0; ph ^= 1; }
         }
@@ -163,8 +176,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
       bool sf_loaded = false;
       long long g = 0;  // stages consumed so far (all tiles)
       for (int t = cluster; t < num_tiles && ok; t += nclusters, ++local) {
+        int tm, tn;
+        tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
+        (void)tm;
+        const int ab = (Cfg::kAccBufs == 2) ? (local & 1) : 0;
+        const uint32_t aph = static_cast<uint32_t>((Cfg::kAccBufs == 2 ? (local >> 1) : local) & 1);
+        const uint32_t d_tmem = tmem_base + ab * TN;
+        const uint32_t sfb_shift = static_cast<uint32_t>(((tn * TN) % 128) / 32);  // 0 or 2 columns
         const long long w1 = tracing ? clock64() : 0;
-        if (!mbar_wait(accempty, (local & 1) ^ 1, wc, 32)) { ok = false; break; }
+        if (!mbar_wait(&accempty[ab], aph ^ 1, wc, 32)) { ok = false; break; }
         if (tracing) tr_b += clock64() - w1;
         tc_fence_after();
         for (int kb = 0; kb < nk; ++kb) {
@@ -200,12 +220,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
             const int j = kk >> 2, k = kk & 3;
             const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
             const uint64_t adesc = sdesc_sw128(aaddr + j * Cfg::kAtom + k * 32, 16, 1024);
-            const uint64_t bdesc = sdesc_sw128(baddr + j * Cfg::kAtom + k * 32, 16, 1024);
+            const uint64_t bdesc = sdesc_sw128(baddr + j * Cfg::kBAtom + k * 32, 16, 1024);
             // MMA kk covers 64 K values = SF blocks 2kk, 2kk+1: atom kk/2, byte (2kk) % 4.
             const uint32_t sf_id = (2 * kk) & 3;
             const uint32_t atom = unit_sf ? 0u : static_cast<uint32_t>(kk >> 1);
-            umma_mxf4_pair(tmem_base, adesc, bdesc, idesc_mxf4(256, 256, sf_id, sf_id),
-                           tmem_sfa + sfb_off + 4 * atom, tmem_sfb + sfb_off + 8 * atom, acc);
+            umma_mxf4_pair(d_tmem, adesc, bdesc, idesc_mxf4(256, TN, sf_id, sf_id),
+                           tmem_sfa + sfb_off + 4 * atom, tmem_sfb + sfb_off + 8 * atom + sfb_shift, acc);
           }
           umma_commit_pair(empty_own + s * 8);
           umma_commit_pair(empty_peer + s * 8);
@@ -214,8 +234,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
           if (++s == kMxStages) { s = 0; ph ^= 1; }
         }
         if (ok) {
-          umma_commit_pair(accfull_own);
-          umma_commit_pair(accfull_peer);
+          umma_commit_pair(accfull_own + ab * 8);
+          umma_commit_pair(accfull_peer + ab * 8);
         }
       }
       umma_commit_pair(smem_u32(teardown));
@@ -253,54 +273,80 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
       }
     }
   } else {
-    // ---------------- epilogue: warps 2..9, lane quarter q, column half h ----------------
+    // ---------------- epilogue ----------------
     const int q = warp & 3;
-    const int h = (warp - 2) >> 2;
     const uint32_t accempty_leader = mapa_shared(smem_u32(accempty), 0);
     float alpha = 1.f;
     if (p.scale_a) alpha *= __ldg(p.scale_a);
     if (p.scale_b) alpha *= __ldg(p.scale_b);
-    int local = 0;
-    for (int t = cluster; t < num_tiles; t += nclusters, ++local) {
-      int tm, tn;
-      tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
-      const long long w3 = tracing ? clock64() : 0;
-      if (!mbar_wait(accfull, local & 1, wc, 35)) break;
-      const long long w4 = tracing ? clock64() : 0;
-      if (tracing) tr_a += w4 - w3;
-      tc_fence_after();
-      uint32_t r[128];
-      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + h * 128;
+    if constexpr (TN == 192) {
+      // warps 2..5: double-buffered accumulators, 32-byte direct stores (warps 6..9 idle)
+      if (warp < 6) {
+        int local = 0;
+        for (int t = cluster; t < num_tiles; t += nclusters, ++local) {
+          int tm, tn;
+          tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
+          const int ab = local & 1;
+          const long long w3 = tracing ? clock64() : 0;
+          if (!mbar_wait(&accfull[ab], static_cast<uint32_t>((local >> 1) & 1), wc, 35)) break;
+          const long long w4 = tracing ? clock64() : 0;
+          if (tracing) tr_a += w4 - w3;
+          tc_fence_after();
+          const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + ab * TN;
+          const int row = tm * TM + static_cast<int>(rank) * 128 + q * 32 + lane;
+          epilogue_tile_direct<OUT, TN>(tbase, p, row, tn * TN, alpha, [&] {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(accempty_leader + ab * 8);
+          });
+          if (tracing) tr_b += clock64() - w4;
+        }
+      }
+    } else {
+      // warps 2..9: lane quarter q, column half h; drain the single accumulator to registers
+      const int h = (warp - 2) >> 2;
+      int local = 0;
+      for (int t = cluster; t < num_tiles; t += nclusters, ++local) {
+        int tm, tn;
+        tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
+        const long long w3 = tracing ? clock64() : 0;
+        if (!mbar_wait(accfull, local & 1, wc, 35)) break;
+        const long long w4 = tracing ? clock64() : 0;
+        if (tracing) tr_a += w4 - w3;
+        tc_fence_after();
+        uint32_t r[128];
+        const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + h * 128;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(tbase + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&r[32 * c]));
-      tmem_ld_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(accempty_leader);  // accumulator free: next tile may start
-      if (tracing) tr_b += clock64() - w4;  // drain time (TMEM -> registers)
-      const int row = tm * TM + static_cast<int>(rank) * 128 + q * 32 + lane;
-      if (row < p.M) {
-        const int col0 = tn * TN + h * 128;
+        for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(tbase + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&r[32 * c]));
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(accempty_leader);  // accumulator free: next tile may start
+        if (tracing) tr_b += clock64() - w4;  // drain time (TMEM -> registers)
+        const int row = tm * TM + static_cast<int>(rank) * 128 + q * 32 + lane;
+        if (row < p.M) {
+          const int col0 = tn * TN + h * 128;
 #pragma unroll
-        for (int g = 0; g < 16; ++g) {  // 16 groups of 8 columns
-          const int col = col0 + 8 * g;
-          if (col >= p.N) break;
-          if constexpr (OUT == Out::F32) {
-            float* dst = reinterpret_cast<float*>(p.C) + static_cast<size_t>(row) * p.ldc + col;
-            uint32_t v[8];
+          for (int g = 0; g < 16; ++g) {  // 16 groups of 8 columns
+            const int col = col0 + 8 * g;
+            if (col >= p.N) break;
+            if constexpr (OUT == Out::F32) {
+              float* dst = reinterpret_cast<float*>(p.C) + static_cast<size_t>(row) * p.ldc + col;
+              uint32_t v[8];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) v[j] = __float_as_uint(__uint_as_float(r[8 * g + j]) * alpha);
-            st_global_v8(dst, v);
-          } else {
-            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.C) + static_cast<size_t>(row) * p.ldc + col;
-            uint32_t v[4];
+              for (int j = 0; j < 8; ++j) v[j] = __float_as_uint(__uint_as_float(r[8 * g + j]) * alpha);
+              st_global_v8(dst, v);
+            } else {
+              __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.C) + static_cast<size_t>(row) * p.ldc + col;
+              uint32_t v[4];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              __nv_bfloat162 b2 = __floats2bfloat162_rn(__uint_as_float(r[8 * g + 2 * j]) * alpha,
-                                                        __uint_as_float(r[8 * g + 2 * j + 1]) * alpha);
-              v[j] = *reinterpret_cast<uint32_t*>(&b2);
+              for (int j = 0; j < 4; ++j) {
+                __nv_bfloat162 b2 = __floats2bfloat162_rn(__uint_as_float(r[8 * g + 2 * j]) * alpha,
+                                                          __uint_as_float(r[8 * g + 2 * j + 1]) * alpha);
+                v[j] = *reinterpret_cast<uint32_t*>(&b2);
+              }
+              *reinterpret_cast<uint4*>(dst) = make_uint4(v[0], v[1], v[2], v[3]);
             }
-            *reinterpret_cast<uint4*>(dst) = make_uint4(v[0], v[1], v[2], v[3]);
           }
         }
       }

@@ -281,17 +281,19 @@ def test_pair_kernel_staged_epilogue_when_c_not_32b_aligned(cuda_dev, kind):
     assert torch.equal(C, ref)
 
 
-MX_PAIR_SHAPES = [(512, 512, 512), (300, 520, 1024), (1024, 768, 800), (2048, 2048, 4096)]
+MX_PAIR_SHAPES = [(512, 512, 512), (300, 520, 1024), (1024, 768, 800), (2048, 2048, 4096), (512, 1344, 512)]
 
 
 @pytest.mark.parametrize("M,N,K", MX_PAIR_SHAPES)
 @pytest.mark.parametrize("out", [bwgemm.OUT_F32, bwgemm.OUT_BF16])
-def test_mxfp4_pair_kernel_parity(cuda_dev, monkeypatch, M, N, K, out):
+@pytest.mark.parametrize("tn", ["192", "256"])
+def test_mxfp4_pair_kernel_parity(cuda_dev, monkeypatch, M, N, K, out, tn):
     """The CTA-pair block-scaled kernel (forced with BW_PAIR=1) against the oracle, including
     M/N tails inside a 256 x 256 tile and K not a multiple of the 512-deep stage."""
     import torch
 
     monkeypatch.setenv("BW_PAIR", "1")
+    monkeypatch.setenv("BW_MX_TN", tn)
     A = o.seeded_normal((M, K), 71)
     B = o.seeded_normal((K, N), 72)
     A[:, :5] *= 100.0  # a few blocks with large scales
