@@ -331,7 +331,7 @@ def run_ours(args, world, rank, local):
         peak_name = f"{mult:.0f} x bf16_tflops (burst)"
     achieved = flops / (ms * 1e-3) / 1e12
     traffic = profile_traffic({"f16": "bw_tc_gemm_pair_f16_8192", "fp8": "bw_tc_gemm_pair_fp8_8192",
-                               "mxfp4": "bw_tc_gemm_mxfp4_8192", "fp4": "bw_tc_gemm_mxfp4_8192"}[wl])
+                               "mxfp4": "bw_tc_gemm_pair_mxfp4_8192", "fp4": "bw_tc_gemm_pair_fp4_8192"}[wl])
     roofline = {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(peak, 1), "unit": "TFLOP/s",
                 "frac": round(achieved / peak, 4), "traffic": traffic,
                 "peak_source": f"{peak_src}: {peak_name}",

@@ -128,6 +128,8 @@ template <Out OUT, int NCOLS, typename Release>
 __device__ __forceinline__ void epilogue_tile_direct(uint32_t tbase, const GemmParams& p, int row, int col0,
                                                      float alpha, Release release) {
   static_assert(NCOLS % 32 == 0, "tile width must be whole 32-column chunks");
+  const bool stream_out = (p.hints & 2) != 0;  // results go out with L2 evict-first priority
+  const uint64_t pol = l2_policy_evict_first();
 #pragma unroll 1
   for (int c = 0; c < NCOLS; c += 32) {
     uint32_t r[32];
@@ -144,7 +146,8 @@ __device__ __forceinline__ void epilogue_tile_direct(uint32_t tbase, const GemmP
         uint32_t v[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) v[j] = __float_as_uint(__uint_as_float(r[8 * g + j]) * alpha);
-        st_global_v8(dst + 8 * g, v);
+        if (stream_out) st_global_v8_hint(dst + 8 * g, v, pol);
+        else st_global_v8(dst + 8 * g, v);
       }
     } else {
       __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.C) + static_cast<size_t>(row) * p.ldc + col;
@@ -159,7 +162,8 @@ __device__ __forceinline__ void epilogue_tile_direct(uint32_t tbase, const GemmP
           v[j] = *reinterpret_cast<uint32_t*>(&h);
         }
         if (col + 16 * g + 16 <= p.N) {
-          st_global_v8(dst + 16 * g, v);
+          if (stream_out) st_global_v8_hint(dst + 16 * g, v, pol);
+          else st_global_v8(dst + 16 * g, v);
         } else {  // N % 16 == 8: the last group holds 8 valid columns
           *reinterpret_cast<uint4*>(dst + 16 * g) = make_uint4(v[0], v[1], v[2], v[3]);
         }

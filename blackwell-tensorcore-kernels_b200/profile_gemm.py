@@ -1,4 +1,4 @@
-"""Small driver for profiling one GEMM kind under ncu: KIND=f16|fp8|mxfp4, N=size (square).
+"""Small driver for profiling one GEMM kind under ncu: KIND=f16|fp8|fp4|mxfp4, N=size (square).
 Runs the GEMM three times (ncu -s 1 -c 1 then captures the second launch).
 
     KIND=f16 N=8192 ncu --set full --clock-control none -k regex:bw_tc_gemm -s 1 -c 1 \
@@ -19,6 +19,9 @@ if kind == 'f16':
 elif kind == 'fp8':
     qa, sa = bwgemm.quantize_fp8(torch.randn(M, K, device=dev)); qb, sb = bwgemm.quantize_fp8(torch.randn(K, N, device=dev), True)
     C = torch.empty(M, N, device=dev, dtype=torch.bfloat16); f = lambda: bwgemm.gemm_fp8(qa, qb, sa, sb, C)
+elif kind == 'fp4':
+    qa, sa = bwgemm.quantize_fp4(torch.randn(M, K, device=dev)); qb, sb = bwgemm.quantize_fp4(torch.randn(K, N, device=dev), True)
+    C = torch.empty(M, N, device=dev, dtype=torch.bfloat16); f = lambda: bwgemm.gemm_fp4(qa, qb, K, sa, sb, C=C)
 else:
     qa, sfa = bwgemm.quantize_mxfp4(torch.randn(M, K, device=dev)); qb, sfb = bwgemm.quantize_mxfp4(torch.randn(K, N, device=dev), True)
     C = torch.empty(M, N, device=dev, dtype=torch.bfloat16); f = lambda: bwgemm.gemm_mxfp4(qa, qb, sfa, sfb, K, C=C)
