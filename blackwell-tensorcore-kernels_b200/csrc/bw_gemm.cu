@@ -28,7 +28,7 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, 
     BW_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
     attr_done[dev & 63] = true;
   }
-  const int tiles = ((p.M + kBM - 1) / kBM) * ((p.N + BN - 1) / BN);
+  const int tiles = ((p.M + kBM - 1) / kBM) * ((p.N + BN - 1) / BN) * (p.splits > 1 ? p.splits : 1);
   int grid = tiles < d.sms ? tiles : d.sms;
   const int cap = env_int("BW_MAX_CTAS", 0);
   if (cap > 0 && grid > cap) grid = cap;
@@ -159,6 +159,8 @@ GemmParams base_params(const DeviceState& d, void* C, int M, int N, int K) {
   p.ldc = N;
   p.group_m = env_int("BW_GROUP_M", 16);
   p.hints = env_int("BW_L2_HINTS", 1);
+  p.splits = 1;
+  p.kb_per_split = 0;
   if (p.group_m < 1) p.group_m = 1;
   p.status = d.status;
   p.budget_ns = wait_budget_ns();
@@ -175,13 +177,18 @@ int check_common(const void* A, const void* B, const void* C, int M, int N, int 
   return BW_OK;
 }
 
-// Skinny problems (one 128-row tile band, many columns) are HBM-bound streams of B: 128 x 64
-// tiles give enough tiles to balance 148 SMs and 8 stages keep ~190 KB of B in flight per SM.
-bool use_skinny(int M, int N, const DeviceState& d) {
-  // Measured slower than the CTA-pair kernel on 128 x 65536 x 8192 (259 vs 230 us): every 64-wide
-  // tile re-reads A from L2. Kept as an explicit option (BW_SKINNY=1) until split-K replaces it.
-  (void)M; (void)N; (void)d;
-  return env_int("BW_SKINNY", 0) != 0;
+// Split-K for HBM-bound short-and-wide problems (M <= 256, e.g. the decode-style 128 x 65536):
+// 128 x 256 single-CTA tiles split along K until there are >= 4 work units per SM, each split
+// >= 8 k-slabs; partial tiles are added into C (zeroed first, in stream order) by the TMA
+// reduce-add store. FP32 output only. Returns the split count (1 = no split).
+int choose_splits(int M, int N, int nk, int out_elem, const DeviceState& d) {
+  const int forced = env_int("BW_SPLITK", -1);
+  if (forced >= 1) return forced;
+  if (forced == 0 || out_elem != 4 || M > 256) return 1;
+  const long tiles = static_cast<long>((M + 127) / 128) * ((N + 255) / 256);
+  int s = 1;
+  while (s < 8 && tiles * s < 4L * d.sms && nk / (2 * s) >= 8) s *= 2;
+  return s;
 }
 
 // Prefer 128 x 256 tiles; fall back to 128 x 128 when the wide tiles would leave SMs idle.
@@ -193,6 +200,16 @@ bool use_narrow(int M, int N, const DeviceState& d) {
   return tiles256 < d.sms;
 }
 
+size_t out_elem_bytes(int out_dtype) { return out_dtype == BW_OUT_BF16 ? 2 : 4; }
+
+// Even k-slab ranges with no empty split.
+int set_splits(GemmParams& p, int splits, int nk) {
+  if (splits < 1 || nk < 1) return set_error(BW_ERR_INVALID, "bad split-K configuration");
+  p.kb_per_split = (nk + splits - 1) / splits;
+  p.splits = (nk + p.kb_per_split - 1) / p.kb_per_split;
+  return BW_OK;
+}
+
 int gemm_f16_impl(const void* A, const void* B, float* C, int M, int N, int K, cudaStream_t s, bool b_mn) {
   int r = check_common(A, B, C, M, N, K);
   if (r != BW_OK || M == 0 || N == 0) return r;
@@ -201,10 +218,10 @@ int gemm_f16_impl(const void* A, const void* B, float* C, int M, int N, int K, c
   DeviceState* d;
   if ((r = ensure_device(&d)) != BW_OK) return r;
   if (K == 0) { BW_CUDA(cudaMemsetAsync(C, 0, sizeof(float) * size_t(M) * N, s)); return BW_OK; }
-  const bool skinny = use_skinny(M, N, *d);
-  const bool pair = !skinny && use_pair(M, N, *d);
-  const bool narrow = !pair && !skinny && use_narrow(M, N, *d);
-  const int bn = skinny ? 64 : pair ? 128 : narrow ? 128 : 256;
+  const int splits = choose_splits(M, N, (K + 63) / 64, 4, *d);
+  const bool pair = splits == 1 && use_pair(M, N, *d);
+  const bool narrow = !pair && splits == 1 && use_narrow(M, N, *d);
+  const int bn = pair ? 128 : narrow ? 128 : 256;
   CUtensorMap ta, tb;
   if ((r = make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, A, K, M, uint64_t(K) * 2, 64, 128)) != BW_OK) return r;
   if (b_mn) r = make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, B, N, K, uint64_t(N) * 2, 64, 64);
@@ -221,9 +238,11 @@ int gemm_f16_impl(const void* A, const void* B, float* C, int M, int N, int K, c
     if (b_mn) return launch_pair<Kind::F16, true, 3, Out::F32, false, 2>(ta, tb, tc, p, s, *d);
     return launch_pair<Kind::F16, false, 3, Out::F32, false, 2>(ta, tb, tc, p, s, *d);
   }
-  if (skinny) {
-    if (b_mn) return launch<Kind::F16, true, 64, 8, 2, Out::F32>(ta, tb, tc, p, s, *d);
-    return launch<Kind::F16, false, 64, 8, 2, Out::F32>(ta, tb, tc, p, s, *d);
+  if (splits > 1) {
+    if ((r = set_splits(p, splits, (K + 63) / 64)) != BW_OK) return r;
+    BW_CUDA(cudaMemsetAsync(C, 0, sizeof(float) * size_t(M) * N, s));
+    if (b_mn) return launch<Kind::F16, true, 256, 4, 2, Out::F32>(ta, tb, tc, p, s, *d);
+    return launch<Kind::F16, false, 256, 4, 2, Out::F32>(ta, tb, tc, p, s, *d);
   }
   if (b_mn) {
     if (narrow) return launch<Kind::F16, true, 128, 6, 2, Out::F32>(ta, tb, tc, p, s, *d);
@@ -232,8 +251,6 @@ int gemm_f16_impl(const void* A, const void* B, float* C, int M, int N, int K, c
   if (narrow) return launch<Kind::F16, false, 128, 6, 2, Out::F32>(ta, tb, tc, p, s, *d);
   return launch<Kind::F16, false, 256, 4, 2, Out::F32>(ta, tb, tc, p, s, *d);
 }
-
-size_t out_elem_bytes(int out_dtype) { return out_dtype == BW_OUT_BF16 ? 2 : 4; }
 
 int gemm_fp8_impl(const uint8_t* A, const uint8_t* Bt, const float* sa, const float* sb, void* C, int out_dtype,
                   int M, int N, int K, cudaStream_t s) {
@@ -245,10 +262,10 @@ int gemm_fp8_impl(const uint8_t* A, const uint8_t* Bt, const float* sa, const fl
   DeviceState* d;
   if ((r = ensure_device(&d)) != BW_OK) return r;
   if (K == 0) { BW_CUDA(cudaMemsetAsync(C, 0, out_elem_bytes(out_dtype) * size_t(M) * N, s)); return BW_OK; }
-  const bool skinny = use_skinny(M, N, *d);
-  const bool pair = !skinny && use_pair(M, N, *d);
-  const bool narrow = !pair && !skinny && use_narrow(M, N, *d);
-  const int bn = skinny ? 64 : pair ? 128 : narrow ? 128 : 256;
+  const int splits = choose_splits(M, N, (K + 127) / 128, static_cast<int>(out_elem_bytes(out_dtype)), *d);
+  const bool pair = splits == 1 && use_pair(M, N, *d);
+  const bool narrow = !pair && splits == 1 && use_narrow(M, N, *d);
+  const int bn = pair ? 128 : narrow ? 128 : 256;
   CUtensorMap ta, tb;
   if ((r = make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, A, K, M, uint64_t(K), 128, 128)) != BW_OK) return r;
   if ((r = make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, Bt, K, N, uint64_t(K), 128, bn)) != BW_OK) return r;
@@ -266,9 +283,10 @@ int gemm_fp8_impl(const uint8_t* A, const uint8_t* Bt, const float* sa, const fl
     if (direct) return launch_pair<Kind::F8, false, 3, Out::BF16, true, 2>(ta, tb, tc, p, s, *d);
     return launch_pair<Kind::F8, false, 3, Out::BF16, false, 2>(ta, tb, tc, p, s, *d);
   }
-  if (skinny) {
-    if (out_dtype == BW_OUT_F32) return launch<Kind::F8, false, 64, 8, 2, Out::F32>(ta, tb, tc, p, s, *d);
-    return launch<Kind::F8, false, 64, 8, 2, Out::BF16>(ta, tb, tc, p, s, *d);
+  if (splits > 1) {  // FP32 output only (choose_splits)
+    if ((r = set_splits(p, splits, (K + 127) / 128)) != BW_OK) return r;
+    BW_CUDA(cudaMemsetAsync(C, 0, sizeof(float) * size_t(M) * N, s));
+    return launch<Kind::F8, false, 256, 4, 2, Out::F32>(ta, tb, tc, p, s, *d);
   }
   if (out_dtype == BW_OUT_F32) {
     if (narrow) return launch<Kind::F8, false, 128, 6, 2, Out::F32>(ta, tb, tc, p, s, *d);

@@ -74,6 +74,8 @@ struct GemmParams {
   const uint8_t* sfb;          // MXF4: B scale factors
   int sf_kgroups;              // MXF4: number of 4-block K groups per 128-row block
   int group_m;                 // raster: tile rows per group
+  int splits;                  // single-CTA kernel: K splits per tile (>1: partials are TMA-reduce-added into zeroed C)
+  int kb_per_split;            // k-slabs per split
   int hints;                   // bit 0: A/B loads evict_last (else evict_normal); bit 1: C stores evict_first
   int* status;                 // device status word
   unsigned long long* trace;   // optional per-CTA wait-time trace (kTraceWords per CTA), or null
@@ -175,7 +177,7 @@ __device__ __forceinline__ void epilogue_tile_direct(uint32_t tbase, const GemmP
 template <Out OUT, int NCOLS, typename Release>
 __device__ __forceinline__ void epilogue_tile(uint32_t tbase, const CUtensorMap* tmC, int x0, int y0, float alpha,
                                               uint8_t* wbuf, int& uses, int lane, uint64_t store_policy,
-                                              bool hinted, Release release) {
+                                              bool hinted, Release release, bool reduce_add = false) {
   constexpr int kCols = (OUT == Out::F32) ? 32 : 64;  // columns per 128-byte row chunk
   static_assert(NCOLS % kCols == 0, "tile width must be whole 128-byte chunks");
   const uint32_t row_addr = smem_u32(wbuf) + lane * 128;
@@ -214,7 +216,8 @@ __device__ __forceinline__ void epilogue_tile(uint32_t tbase, const CUtensorMap*
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) {
-      if (hinted) tma_store_2d_hint(tmC, wbuf + bsel * kEpiBufBytes, x0 + c, y0, store_policy);
+      if (reduce_add) tma_reduce_add_2d(tmC, wbuf + bsel * kEpiBufBytes, x0 + c, y0);
+      else if (hinted) tma_store_2d_hint(tmC, wbuf + bsel * kEpiBufBytes, x0 + c, y0, store_policy);
       else tma_store_2d(tmC, wbuf + bsel * kEpiBufBytes, x0 + c, y0);
       bulk_commit_group();
     }
@@ -245,7 +248,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tiles_m = (p.M + kBM - 1) / kBM;
   const int tiles_n = (p.N + BN - 1) / BN;
   const int num_tiles = tiles_m * tiles_n;
-  const int nk = (p.K + KE - 1) / KE;
+  const int nk_all = (p.K + KE - 1) / KE;
+  // Work unit u = (tile u / splits, K split u % splits): k-slabs [kb0, kb1) of that tile.
+  const int splits = p.splits > 1 ? p.splits : 1;
+  const int kb_per = splits > 1 ? p.kb_per_split : nk_all;
+  const int num_units = num_tiles * splits;
   const WaitCtl wc{abort_flag, p.status, p.budget_ns};
 
   if constexpr (KIND == Kind::MXF4) {
@@ -279,10 +286,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       int s = 0;
       uint32_t ph = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
         int tm, tn;
-        tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
-        for (int kb = 0; kb < nk; ++kb) {
+        tile_coords(u / splits, tiles_m, tiles_n, p.group_m, tm, tn);
+        const int kb0 = (u % splits) * kb_per, kb1 = min(nk_all, kb0 + kb_per);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[s], ph ^ 1, wc, 1)) { ok = false; break; }
           uint8_t* sA = smem + s * Cfg::kStageBytes;
           uint8_t* sB = sA + Cfg::kABytes;
@@ -333,18 +341,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t ph = 0;
       int local = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++local) {
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x, ++local) {
         const int b = local % ACC_BUFS;
         const uint32_t aph = (local / ACC_BUFS) & 1;
+        const int kb0 = (u % splits) * kb_per, kb1 = min(nk_all, kb0 + kb_per);
         if (!mbar_wait(&accempty[b], aph ^ 1, wc, 2)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + b * BN;
-        for (int kb = 0; kb < nk; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[s], ph, wc, 3)) { ok = false; break; }
           tc_fence_after();
           const uint32_t aaddr = smem_u32(smem + s * Cfg::kStageBytes);
           const uint32_t baddr = aaddr + Cfg::kABytes;
-          if (KIND == Kind::MXF4 && (p.sfa != nullptr || (kb == 0 && local == 0))) {
+          if (KIND == Kind::MXF4 && (p.sfa != nullptr || (kb == kb0 && local == 0))) {
             // Per-slab scale factors; with no SF arrays (plain FP4) the 0x7f-filled slots are
             // copied once and every block scale stays 2^0.
             const uint32_t sfa_s = baddr + Cfg::kBBytes;
@@ -361,7 +370,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
+            const uint32_t acc = (kb > kb0 || k > 0) ? 1u : 0u;
             const uint64_t adesc = sdesc_sw128(aaddr + k * 32, 16, 1024);
             uint64_t bdesc;
             if constexpr (B_MN) bdesc = sdesc_sw128(baddr + k * 16 * kSlabBytes, 64 * kSlabBytes, 1024);
@@ -397,9 +406,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (p.scale_a) alpha *= __ldg(p.scale_a);
     if (p.scale_b) alpha *= __ldg(p.scale_b);
     int local = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
+    for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++local) {
       int tm, tn;
-      tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
+      tile_coords(u / splits, tiles_m, tiles_n, p.group_m, tm, tn);
       const int b = local % ACC_BUFS;
       const uint32_t aph = (local / ACC_BUFS) & 1;
       if (!mbar_wait(&accfull[b], aph, wc, 5)) break;
@@ -409,7 +418,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                              (p.hints & 2) != 0, [&] {
         tc_fence_before();
         mbar_arrive(&accempty[b]);
-      });
+      }, splits > 1);
     }
     if (lane == 0) bulk_wait_group<0>();
   }

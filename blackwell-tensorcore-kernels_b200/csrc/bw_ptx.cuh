@@ -344,6 +344,13 @@ __device__ __forceinline__ void tma_store_2d_hint(const CUtensorMap* m, const vo
                "r"(smem_u32(src)), "r"(x), "r"(y), "l"(policy)
                : "memory");
 }
+// TMA reduce: element-wise add of the shared-memory box into global memory (split-K partials).
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* m, const void* src, int x, int y) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
 template <int N>
 __device__ __forceinline__ void bulk_wait_group_read() {
   asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");

@@ -332,13 +332,15 @@ def test_fp4_pair_kernel_parity(cuda_dev, monkeypatch, M, N, K, out):
     assert np.abs(C - R).max() <= tol
 
 
-@pytest.mark.parametrize("M,N,K", [(128, 4096, 1024), (77, 2056, 520), (1, 1024, 64)])
+@pytest.mark.parametrize("M,N,K", [(128, 4096, 1024), (77, 2056, 528), (200, 1024, 4096), (1, 1024, 1024)])
 @pytest.mark.parametrize("kind", ["f16", "fp8"])
-def test_skinny_kernel_parity(cuda_dev, monkeypatch, M, N, K, kind):
-    """The 128 x 64 single-CTA path for one-band (decode-style) shapes, forced with BW_SKINNY=1."""
+@pytest.mark.parametrize("splits", ["2", "3", "8"])
+def test_splitk_parity(cuda_dev, monkeypatch, M, N, K, kind, splits):
+    """Split-K (partial tiles TMA-reduce-added into zeroed C), forced with BW_SPLITK; uneven
+    k-slab ranges and more splits than k-slabs included."""
     import torch
 
-    monkeypatch.setenv("BW_SKINNY", "1")
+    monkeypatch.setenv("BW_SPLITK", splits)
     if kind == "f16":
         A = _f16(o.seeded_uniform((M, K), 91))
         B = _f16(o.seeded_uniform((K, N), 92))
