@@ -277,6 +277,7 @@ def run_ours(args, world, rank, local):
         # untimed by the headline: NCCL all-gather of the C shards into row-major M x (N world)
         import sharding
 
+        sharding.gather_columns(C, world)  # warm-up: NCCL communicator and buffers
         torch.cuda.synchronize()
         barrier(world)
         g0 = torch.cuda.Event(enable_timing=True)
