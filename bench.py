@@ -414,8 +414,17 @@ def compare_rows(args, wl, inp, dev, stream):
                         lambda: torch._scaled_mm(a8, b8, scale_a=sa, scale_b=sb, out_dtype=torch.bfloat16))
             q4a, sfa = bwgemm.quantize_mxfp4(A32, False, bwgemm.MX_BLOCK32)
             q4b, sfb = bwgemm.quantize_mxfp4(B32, True, bwgemm.MX_BLOCK32)
-            out["ours_mxfp4_bf16out_tflops"] = round(
-                tf(lambda: bwgemm.gemm_mxfp4(q4a, q4b, sfa, sfb, K, C=C8, stream=stream)), 1)
+            F = torch.nn.functional
+            a4 = q4a.view(torch.float4_e2m1fn_x2)
+            b4 = q4b.view(torch.float4_e2m1fn_x2).t()
+            e8a = sfa.view(torch.float8_e8m0fnu)
+            e8b = sfb.view(torch.float8_e8m0fnu)
+            interleaved("ours_mxfp4_bf16out_tflops",
+                        lambda: bwgemm.gemm_mxfp4(q4a, q4b, sfa, sfb, K, C=C8, stream=stream),
+                        "cublaslt_mxfp4_bf16out_tflops",
+                        lambda: F.scaled_mm(a4, b4, e8a, F.ScalingType.BlockWise1x32, e8b,
+                                            F.ScalingType.BlockWise1x32, swizzle_a=F.SwizzleType.SWIZZLE_32_4_4,
+                                            swizzle_b=F.SwizzleType.SWIZZLE_32_4_4, output_dtype=torch.bfloat16))
             out["block_steps"] = block
     except Exception as ex:  # a missing library path must not hide the headline number
         out["error"] = f"{type(ex).__name__}: {ex}"[:200]

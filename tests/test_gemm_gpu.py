@@ -384,3 +384,28 @@ def test_fp8_pair_bf16_out_with_unaligned_row_pitch(cuda_dev, monkeypatch, N):
     R = o.gemm_f64(o.dequant_fp8(ra), o.dequant_fp8(rb), b_trans=True) * float(np.float32(rsa) * np.float32(rsb))
     tol = o.lowp_tolerance(K, 448 * rsa, 448 * rsb, np.abs(R).max(), True)
     assert np.abs(C - R).max() <= tol
+
+
+@pytest.mark.parametrize("M,N,K", [(1024, 1024, 1024), (4096, 4096, 2048)])
+def test_mxfp4_bit_identical_to_cublaslt(cuda_dev, M, N, K):
+    """Independent check of the block-scaled path: cuBLASLt's MXFP4 GEMM (through
+    torch.nn.functional.scaled_mm, BlockWise1x32 with the 32x4x4-swizzled UE8M0 layout, which
+    is our scale-factor layout) on the very same quantised buffers gives the same BF16 bits."""
+    import torch
+
+    F = torch.nn.functional
+    if not hasattr(F, "scaled_mm") or not hasattr(torch, "float4_e2m1fn_x2"):
+        pytest.skip("torch build without block-scaled FP4 scaled_mm")
+    A = torch.randn(M, K, device=cuda_dev)
+    B = torch.randn(K, N, device=cuda_dev)
+    qa, sfa = bwgemm.quantize_mxfp4(A, False, bwgemm.MX_BLOCK32)
+    qb, sfb = bwgemm.quantize_mxfp4(B, True, bwgemm.MX_BLOCK32)
+    ours = bwgemm.gemm_mxfp4(qa, qb, sfa, sfb, K, out_dtype=bwgemm.OUT_BF16)
+    lib = F.scaled_mm(qa.view(torch.float4_e2m1fn_x2), qb.view(torch.float4_e2m1fn_x2).t(),
+                      sfa.view(torch.float8_e8m0fnu), F.ScalingType.BlockWise1x32,
+                      sfb.view(torch.float8_e8m0fnu), F.ScalingType.BlockWise1x32,
+                      swizzle_a=F.SwizzleType.SWIZZLE_32_4_4, swizzle_b=F.SwizzleType.SWIZZLE_32_4_4,
+                      output_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    _status_ok()
+    assert torch.equal(ours, lib)
