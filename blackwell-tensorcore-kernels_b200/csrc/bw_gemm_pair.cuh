@@ -213,7 +213,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       auto release = [&] {
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(accempty_leader + b * 8);
+        if (lane == 0) mbar_arrive_remote_cta(accempty_leader + b * 8);
       };
       const int row0 = tm * TM + static_cast<int>(rank) * 128 + q * 32;
       if constexpr (DIRECT_EPI) epilogue_tile_direct<OUT, TN>(tbase, p, row0 + lane, tn * TN, alpha, release);

@@ -38,8 +38,9 @@ struct MxPairCfg {
   static constexpr int kSfbBytes = 2 * kSfaBytes;          // two 128-row blocks of B
   static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;
   static constexpr int kBarOffset = kMxStages * kStageBytes;
-  // full[S], empty[S], accfull[2], accempty[2], teardown, sf_ready[2], sf_free[2]
-  static constexpr int kNumBars = 2 * kMxStages + 5 + 4;
+  static constexpr int kSfBufs = TN == 256 ? 3 : 2;         // TMEM scale-factor buffers
+  // full[S], empty[S], accfull[2], accempty[2], teardown, sf_ready[kSfBufs], sf_free[kSfBufs]
+  static constexpr int kNumBars = 2 * kMxStages + 5 + 2 * kSfBufs;
   static constexpr int kSmemBytes = kBarOffset + kNumBars * 8 + 16 + 1024;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
   static constexpr int kSfaCols = 4 * kMxKsub * 2;          // 4 atoms per stage x 4 columns
@@ -47,7 +48,7 @@ struct MxPairCfg {
   static constexpr int kSfCols = kSfaCols + kSfbCols;       // 48 per buffer
   static constexpr int kSfBase = kAccBufs * TN;            // first scale-factor column
   static constexpr int kTmemCols = 512;
-  static_assert(kSfBase + 2 * kSfCols <= kTmemCols, "TMEM budget");
+  static_assert(kSfBase + kSfBufs * kSfCols <= kTmemCols, "TMEM budget");
 };
 
 template <Out OUT, int TN>
@@ -67,8 +68,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
   uint64_t* accfull = bars + 2 * kMxStages;
   uint64_t* accempty = accfull + 2;
   uint64_t* teardown = accfull + 4;
-  uint64_t* sf_ready = accfull + 5;  // [2]: scale factors of a stage are in TMEM buffer b
-  uint64_t* sf_free = accfull + 7;   // [2]: the MMAs reading TMEM buffer b have completed
+  uint64_t* sf_ready = accfull + 5;                // [kSfBufs]: a stage's scale factors are in buffer b
+  uint64_t* sf_free = sf_ready + Cfg::kSfBufs;     // [kSfBufs]: the MMAs reading buffer b have completed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -87,7 +88,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
   const WaitCtl wc{abort_flag, p.status, p.budget_ns};
   const long long t_start = clock64();
   const bool tracing = p.trace != nullptr;
-  unsigned long long tr_a = 0, tr_b = 0;
+  unsigned long long tr_a = 0, tr_b = 0, tr_c = 0;
+  long long t_commit = 0;
 
   // Scale-factor slots start at 2^0 (0x7f): the plain-FP4 path copies them once.
   for (int s = 0; s < kMxStages; ++s) {
@@ -102,7 +104,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
       mbar_init(&accempty[b], 2 * (TN == 192 ? 4 : 8));  // epilogue warps of both CTAs
     }
     mbar_init(teardown, 1);
-    for (int b = 0; b < 2; ++b) { mbar_init(&sf_ready[b], 1); mbar_init(&sf_free[b], 1); }
+    for (int b = 0; b < Cfg::kSfBufs; ++b) { mbar_init(&sf_ready[b], 1); mbar_init(&sf_free[b], 1); }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -174,7 +176,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
       int local = 0;
       bool ok = true;
       bool sf_loaded = false;
-      long long g = 0;  // stages consumed so far (all tiles)
+      int sb = 0;         // scale-factor buffer of the next stage
+      uint32_t sph = 0;   // its phase
       for (int t = cluster; t < num_tiles && ok; t += nclusters, ++local) {
         int tm, tn;
         tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
@@ -185,7 +188,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
         const uint32_t sfb_shift = static_cast<uint32_t>(((tn * TN) % 128) / 32);  // 0 or 2 columns
         const long long w1 = tracing ? clock64() : 0;
         if (!mbar_wait(&accempty[ab], aph ^ 1, wc, 32)) { ok = false; break; }
-        if (tracing) tr_b += clock64() - w1;
+        if (tracing) { tr_b += clock64() - w1; if (t_commit) tr_c += clock64() - t_commit; }
         tc_fence_after();
         for (int kb = 0; kb < nk; ++kb) {
           const long long w2 = tracing ? clock64() : 0;
@@ -209,11 +212,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
               sf_loaded = true;
             }
           } else {
-            // the copier warp has put this stage's scale factors into buffer (g & 1)
-            const int b = static_cast<int>(g & 1);
-            if (!mbar_wait(&sf_ready[b], static_cast<uint32_t>((g >> 1) & 1), wc, 36)) { ok = false; break; }
+            // the copier warp has put this stage's scale factors into buffer sb
+            if (!mbar_wait(&sf_ready[sb], sph, wc, 36)) { ok = false; break; }
             tc_fence_after();
-            sfb_off = b * Cfg::kSfCols;
+            sfb_off = sb * Cfg::kSfCols;
           }
 #pragma unroll
           for (int kk = 0; kk < 4 * kMxKsub; ++kk) {
@@ -229,11 +231,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
           }
           umma_commit_pair(empty_own + s * 8);
           umma_commit_pair(empty_peer + s * 8);
-          if (!unit_sf) umma_commit_pair(smem_u32(&sf_free[g & 1]));
-          ++g;
+          if (!unit_sf) {
+            umma_commit_pair(smem_u32(&sf_free[sb]));
+            if (++sb == Cfg::kSfBufs) { sb = 0; sph ^= 1; }
+          }
           if (++s == kMxStages) { s = 0; ph ^= 1; }
         }
         if (ok) {
+          if (tracing) t_commit = clock64();
           umma_commit_pair(accfull_own + ab * 8);
           umma_commit_pair(accfull_peer + ab * 8);
         }
@@ -248,12 +253,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
     if (leader && lane == 0 && !unit_sf) {
       int s = 0;
       uint32_t ph = 0;
-      long long g = 0;
+      int b = 0;
+      uint32_t u = 0;
       bool ok = true;
       for (int t = cluster; t < num_tiles && ok; t += nclusters) {
-        for (int kb = 0; kb < nk; ++kb, ++g) {
-          const int b = static_cast<int>(g & 1);
-          const uint32_t u = static_cast<uint32_t>((g >> 1) & 1);
+        for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&full[s], ph, wc, 37)) { ok = false; break; }
           if (!mbar_wait(&sf_free[b], u ^ 1, wc, 38)) { ok = false; break; }
           tc_fence_after();
@@ -268,6 +272,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
                                         sdesc_noswz(sfb_s + Cfg::kSfaBytes + 512 * a, 16, 128));
           }
           umma_commit_pair(smem_u32(&sf_ready[b]));
+          if (++b == Cfg::kSfBufs) { b = 0; u ^= 1; }
           if (++s == kMxStages) { s = 0; ph ^= 1; }
         }
       }
@@ -297,7 +302,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
           epilogue_tile_direct<OUT, TN>(tbase, p, row, tn * TN, alpha, [&] {
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(accempty_leader + ab * 8);
+            if (lane == 0) mbar_arrive_remote_cta(accempty_leader + ab * 8);
           });
           if (tracing) tr_b += clock64() - w4;
         }
@@ -319,9 +324,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
 #pragma unroll
         for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(tbase + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&r[32 * c]));
         tmem_ld_wait();
+        if (tracing) tr_c += clock64() - w4;
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(accempty_leader);  // accumulator free: next tile may start
+        // accumulator free: the next tile may start. The loads above have completed
+        // (wait::ld), so a CTA-scope release suffices; a cluster-scope release here cost
+        // about 1.5k cycles per tile with the MMA idle.
+        if (lane == 0) mbar_arrive_remote_cta(accempty_leader);
         if (tracing) tr_b += clock64() - w4;  // drain time (TMEM -> registers)
         const int row = tm * TM + static_cast<int>(rank) * 128 + q * 32 + lane;
         if (row < p.M) {
@@ -356,8 +365,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
   if (tracing && lane == 0) {
     unsigned long long* tr = p.trace + static_cast<size_t>(blockIdx.x) * kTraceWords;
     if (warp == 0) tr[3] = tr_a;
-    if (warp == 1 && leader) { tr[1] = tr_a; tr[2] = tr_b; }
-    if (warp == 2) { tr[4] = tr_a; tr[5] = tr_b; }
+    if (warp == 1 && leader) { tr[1] = tr_a; tr[2] = tr_b; tr[6] = tr_c; }
+    if (warp == 2) { tr[4] = tr_a; tr[5] = tr_b; tr[7] = tr_c; }
   }
   tc_fence_before();
   cluster_sync();
