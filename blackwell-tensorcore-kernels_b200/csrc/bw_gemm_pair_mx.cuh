@@ -18,9 +18,10 @@
 
 namespace bw {
 
-constexpr int kMxThreads = 352;  // producer, MMA, 8 epilogue warps, scale-factor copier
+constexpr int kMxThreads = 384;  // producer, MMA, 8 epilogue warps, scale-factor copier and loader
 constexpr int kMxKsub = 2;
-constexpr int kMxStages = 3;
+constexpr int kMxStages = 3;     // A/B stages
+constexpr int kMxSfSlots = 4;    // scale-factor stages in shared memory (run ahead of A/B)
 
 // TN = 256: one 256-column accumulator, 8 epilogue warps drain it to registers.
 // TN = 192: two 192-column accumulators (epilogue overlaps the next tile), 4 epilogue warps
@@ -36,11 +37,14 @@ struct MxPairCfg {
   static constexpr int kBBytes = kMxKsub * kBAtom;         // 32 or 24 KB
   static constexpr int kSfaBytes = kMxKsub * 1024;         // 2 SF atoms (512 B) per K atom of 256
   static constexpr int kSfbBytes = 2 * kSfaBytes;          // two 128-row blocks of B
-  static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;
-  static constexpr int kBarOffset = kMxStages * kStageBytes;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kSfSlotBytes = kSfaBytes + kSfbBytes;
+  static constexpr int kSfRingOffset = kMxStages * kStageBytes;
+  static constexpr int kBarOffset = kSfRingOffset + kMxSfSlots * kSfSlotBytes;
   static constexpr int kSfBufs = TN == 256 ? 3 : 2;         // TMEM scale-factor buffers
-  // full[S], empty[S], accfull[2], accempty[2], teardown, sf_ready[kSfBufs], sf_free[kSfBufs]
-  static constexpr int kNumBars = 2 * kMxStages + 5 + 2 * kSfBufs;
+  // full[S], empty[S], accfull[2], accempty[2], teardown, sf_ready[kSfBufs], sf_free[kSfBufs],
+  // sf_full[kMxSfSlots], sf_empty[kMxSfSlots]
+  static constexpr int kNumBars = 2 * kMxStages + 5 + 2 * kSfBufs + 2 * kMxSfSlots;
   static constexpr int kSmemBytes = kBarOffset + kNumBars * 8 + 16 + 1024;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
   static constexpr int kSfaCols = 4 * kMxKsub * 2;          // 4 atoms per stage x 4 columns
@@ -70,6 +74,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
   uint64_t* teardown = accfull + 4;
   uint64_t* sf_ready = accfull + 5;                // [kSfBufs]: a stage's scale factors are in buffer b
   uint64_t* sf_free = sf_ready + Cfg::kSfBufs;     // [kSfBufs]: the MMAs reading buffer b have completed
+  uint64_t* sf_full = sf_free + Cfg::kSfBufs;      // [slots] (leader): both CTAs' scale factors landed
+  uint64_t* sf_empty = sf_full + kMxSfSlots;       // [slots] (each): the copies out of the slot are done
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -91,20 +97,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
   unsigned long long tr_a = 0, tr_b = 0, tr_c = 0;
   long long t_commit = 0;
 
-  // Scale-factor slots start at 2^0 (0x7f): the plain-FP4 path copies them once.
-  for (int s = 0; s < kMxStages; ++s) {
-    uint32_t* sf = reinterpret_cast<uint32_t*>(smem + s * Cfg::kStageBytes + Cfg::kABytes + Cfg::kBBytes);
-    for (int i = threadIdx.x; i < (Cfg::kSfaBytes + Cfg::kSfbBytes) / 4; i += kMxThreads) sf[i] = 0x7f7f7f7fu;
+  // Scale-factor slot 0 starts at 2^0 (0x7f): the plain-FP4 path copies it once.
+  if (unit_sf) {
+    uint32_t* sf = reinterpret_cast<uint32_t*>(smem + Cfg::kSfRingOffset);
+    for (int i = threadIdx.x; i < Cfg::kSfSlotBytes / 4; i += kMxThreads) sf[i] = 0x7f7f7f7fu;
+    fence_proxy_async_smem();
   }
-  fence_proxy_async_smem();
   if (threadIdx.x == 0) {
     for (int s = 0; s < kMxStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&accfull[b], 1);
       mbar_init(&accempty[b], 2 * (TN == 192 ? 4 : 8));  // epilogue warps of both CTAs
     }
-    mbar_init(teardown, 1);
+    mbar_init(teardown, unit_sf ? 1 : 2);  // MMA thread and scale-factor copier
     for (int b = 0; b < Cfg::kSfBufs; ++b) { mbar_init(&sf_ready[b], 1); mbar_init(&sf_free[b], 1); }
+    for (int b = 0; b < kMxSfSlots; ++b) { mbar_init(&sf_full[b], 1); mbar_init(&sf_empty[b], 1); }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -127,7 +134,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
     if (lane == 0) {
       const uint64_t pol = l2_policy_evict_last();
       const uint32_t full_leader = mapa_shared(smem_u32(full), 0);
-      const uint32_t stage_tx = unit_sf ? (Cfg::kABytes + Cfg::kBBytes) : Cfg::kStageBytes;
+      const uint32_t stage_tx = Cfg::kStageBytes;
       int s = 0;
       uint32_t ph = 0;
       bool ok = true;
@@ -136,15 +143,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
         tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
         const int arow = tm * TM + static_cast<int>(rank) * 128;
         const int bcol = tn * TN + static_cast<int>(rank) * (TN / 2);
-        const int sfb_block = (tn * TN) / 128;  // first 128-row SF block the tile's B rows touch
         for (int kb = 0; kb < nk; ++kb) {
           const long long w0 = tracing ? clock64() : 0;
           if (!mbar_wait(&empty[s], ph ^ 1, wc, 31)) { ok = false; break; }
           if (tracing) tr_a += clock64() - w0;
           uint8_t* sA = smem + s * Cfg::kStageBytes;
           uint8_t* sB = sA + Cfg::kABytes;
-          uint8_t* sSfa = sB + Cfg::kBBytes;
-          uint8_t* sSfb = sSfa + Cfg::kSfaBytes;
           if (leader) mbar_arrive_expect_tx(&full[s], 2 * stage_tx);
           const uint32_t fb = full_leader + s * 8;
 #pragma unroll
@@ -152,15 +156,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
             const int ka = kb * kMxKsub + j;
             tma_load_2d_pair(&tmA, fb, sA + j * Cfg::kAtom, ka * KX, arow, pol);
             tma_load_2d_pair(&tmB, fb, sB + j * Cfg::kBAtom, ka * KX, bcol, pol);
-          }
-          if (!unit_sf) {
-            // SF buffers viewed as rows of 256 B (an atom = 2 rows); a stage needs 4 atoms
-            // (k groups 4kb..4kb+3) of one row block: one 8-row box. Boxes past the end of a
-            // row block read the next block's scales for zero-filled K, past the buffer zeros.
-            const int kg0 = kb * 4;
-            tma_load_2d_pair(&tmSfa, fb, sSfa, 0, ((tm * 2 + static_cast<int>(rank)) * p.sf_kgroups + kg0) * 2, pol);
-            tma_load_2d_pair(&tmSfb, fb, sSfb, 0, (sfb_block * p.sf_kgroups + kg0) * 2, pol);
-            tma_load_2d_pair(&tmSfb, fb, sSfb + Cfg::kSfaBytes, 0, ((sfb_block + 1) * p.sf_kgroups + kg0) * 2, pol);
           }
           if (++s == kMxStages) { s = 0; ph ^= 1; }
         }
@@ -197,11 +192,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
           tc_fence_after();
           const uint32_t aaddr = smem_u32(smem + s * Cfg::kStageBytes);
           const uint32_t baddr = aaddr + Cfg::kABytes;
-          const uint32_t sfa_s = baddr + Cfg::kBBytes;
-          const uint32_t sfb_s = sfa_s + Cfg::kSfaBytes;
           uint32_t sfb_off = 0;  // column offset of the stage's scale-factor buffer
           if (unit_sf) {
-            if (!sf_loaded) {  // plain FP4: the 0x7f slots of stage 0, copied once
+            if (!sf_loaded) {  // plain FP4: the 0x7f scale-factor slot 0, copied once
+              const uint32_t sfa_s = smem_u32(smem + Cfg::kSfRingOffset);
+              const uint32_t sfb_s = sfa_s + Cfg::kSfaBytes;
 #pragma unroll
               for (int a = 0; a < 4; ++a) {
                 tmem_cp_32x128b_warpx4_pair(tmem_sfa + 4 * a, sdesc_noswz(sfa_s + 512 * a, 16, 128));
@@ -249,8 +244,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
   } else if (warp == 10) {
     // ---------------- scale-factor copier (leader only) ----------------
     // Moves each stage's scale factors shared memory -> TMEM (both CTAs, cta_group::2) into
-    // one of two column buffers, so the MMA thread issues only MMAs and commits.
+    // one of kSfBufs column buffers, so the MMA thread issues only MMAs and commits. The
+    // scale factors have their own shared-memory ring, so this runs ahead of the A/B data.
     if (leader && lane == 0 && !unit_sf) {
+      const uint32_t sf_empty_own = smem_u32(sf_empty), sf_empty_peer = mapa_shared(smem_u32(sf_empty), peer);
       int s = 0;
       uint32_t ph = 0;
       int b = 0;
@@ -258,10 +255,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
       bool ok = true;
       for (int t = cluster; t < num_tiles && ok; t += nclusters) {
         for (int kb = 0; kb < nk; ++kb) {
-          if (!mbar_wait(&full[s], ph, wc, 37)) { ok = false; break; }
+          if (!mbar_wait(&sf_full[s], ph, wc, 37)) { ok = false; break; }
           if (!mbar_wait(&sf_free[b], u ^ 1, wc, 38)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t sfa_s = smem_u32(smem + s * Cfg::kStageBytes) + Cfg::kABytes + Cfg::kBBytes;
+          const uint32_t sfa_s = smem_u32(smem + Cfg::kSfRingOffset + s * Cfg::kSfSlotBytes);
           const uint32_t sfb_s = sfa_s + Cfg::kSfaBytes;
           const uint32_t off = b * Cfg::kSfCols;
 #pragma unroll
@@ -272,8 +269,40 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
                                         sdesc_noswz(sfb_s + Cfg::kSfaBytes + 512 * a, 16, 128));
           }
           umma_commit_pair(smem_u32(&sf_ready[b]));
+          umma_commit_pair(sf_empty_own + s * 8);   // slot s may be refilled (both CTAs)
+          umma_commit_pair(sf_empty_peer + s * 8);
           if (++b == Cfg::kSfBufs) { b = 0; u ^= 1; }
-          if (++s == kMxStages) { s = 0; ph ^= 1; }
+          if (++s == kMxSfSlots) { s = 0; ph ^= 1; }
+        }
+      }
+      umma_commit_pair(smem_u32(teardown));  // its commits to the peer land before teardown
+    }
+  } else if (warp == 11) {
+    // ---------------- scale-factor loader (both CTAs) ----------------
+    if (lane == 0 && !unit_sf) {
+      const uint64_t pol = l2_policy_evict_last();
+      const uint32_t sf_full_leader = mapa_shared(smem_u32(sf_full), 0);
+      int s = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int t = cluster; t < num_tiles && ok; t += nclusters) {
+        int tm, tn;
+        tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
+        const int sfb_block = (tn * TN) / 128;  // first 128-row SF block the tile's B rows touch
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&sf_empty[s], ph ^ 1, wc, 39)) { ok = false; break; }
+          uint8_t* sSfa = smem + Cfg::kSfRingOffset + s * Cfg::kSfSlotBytes;
+          uint8_t* sSfb = sSfa + Cfg::kSfaBytes;
+          if (leader) mbar_arrive_expect_tx(&sf_full[s], 2 * Cfg::kSfSlotBytes);
+          const uint32_t fb = sf_full_leader + s * 8;
+          // SF buffers viewed as rows of 256 B (an atom = 2 rows); a stage needs 4 atoms
+          // (k groups 4kb..4kb+3) of one row block: one 8-row box. Boxes past the end of a
+          // row block read the next block's scales for zero-filled K, past the buffer zeros.
+          const int kg0 = kb * 4;
+          tma_load_2d_pair(&tmSfa, fb, sSfa, 0, ((tm * 2 + static_cast<int>(rank)) * p.sf_kgroups + kg0) * 2, pol);
+          tma_load_2d_pair(&tmSfb, fb, sSfb, 0, (sfb_block * p.sf_kgroups + kg0) * 2, pol);
+          tma_load_2d_pair(&tmSfb, fb, sSfb + Cfg::kSfaBytes, 0, ((sfb_block + 1) * p.sf_kgroups + kg0) * 2, pol);
+          if (++s == kMxSfSlots) { s = 0; ph ^= 1; }
         }
       }
     }
@@ -310,6 +339,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
     } else {
       // warps 2..9: lane quarter q, column half h; drain the single accumulator to registers
       const int h = (warp - 2) >> 2;
+      // BF16 rows go out as 32-byte stores when C and its row pitch allow them
+      const bool bf16_v8 = (reinterpret_cast<uintptr_t>(p.C) & 31u) == 0 && (p.ldc % 16) == 0;
       int local = 0;
       for (int t = cluster; t < num_tiles; t += nclusters, ++local) {
         int tm, tn;
@@ -335,26 +366,36 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
         const int row = tm * TM + static_cast<int>(rank) * 128 + q * 32 + lane;
         if (row < p.M) {
           const int col0 = tn * TN + h * 128;
+          if constexpr (OUT == Out::F32) {
 #pragma unroll
-          for (int g = 0; g < 16; ++g) {  // 16 groups of 8 columns
-            const int col = col0 + 8 * g;
-            if (col >= p.N) break;
-            if constexpr (OUT == Out::F32) {
+            for (int g = 0; g < 16; ++g) {  // 16 groups of 8 columns, one 32-byte store each
+              const int col = col0 + 8 * g;
+              if (col >= p.N) break;
               float* dst = reinterpret_cast<float*>(p.C) + static_cast<size_t>(row) * p.ldc + col;
               uint32_t v[8];
 #pragma unroll
               for (int j = 0; j < 8; ++j) v[j] = __float_as_uint(__uint_as_float(r[8 * g + j]) * alpha);
               st_global_v8(dst, v);
-            } else {
-              __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.C) + static_cast<size_t>(row) * p.ldc + col;
-              uint32_t v[4];
+            }
+          } else {
+            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.C) + static_cast<size_t>(row) * p.ldc + col0;
 #pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                __nv_bfloat162 b2 = __floats2bfloat162_rn(__uint_as_float(r[8 * g + 2 * j]) * alpha,
-                                                          __uint_as_float(r[8 * g + 2 * j + 1]) * alpha);
+            for (int g = 0; g < 8; ++g) {  // 8 groups of 16 columns
+              const int col = col0 + 16 * g;
+              if (col >= p.N) break;
+              uint32_t v[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                __nv_bfloat162 b2 = __floats2bfloat162_rn(__uint_as_float(r[16 * g + 2 * j]) * alpha,
+                                                          __uint_as_float(r[16 * g + 2 * j + 1]) * alpha);
                 v[j] = *reinterpret_cast<uint32_t*>(&b2);
               }
-              *reinterpret_cast<uint4*>(dst) = make_uint4(v[0], v[1], v[2], v[3]);
+              if (bf16_v8 && col + 16 <= p.N) {
+                st_global_v8(dst + 16 * g, v);  // full 32-byte sector
+              } else {
+                *reinterpret_cast<uint4*>(dst + 16 * g) = make_uint4(v[0], v[1], v[2], v[3]);
+                if (col + 8 < p.N) *reinterpret_cast<uint4*>(dst + 16 * g + 8) = make_uint4(v[4], v[5], v[6], v[7]);
+              }
             }
           }
         }
