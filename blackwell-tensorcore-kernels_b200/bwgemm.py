@@ -27,6 +27,16 @@ OUT_F32, OUT_BF16 = 0, 1
 SCALE_NONE, SCALE_FIXED8, SCALE_AMAX = 0, 1, 2
 FP4_PACKED, FP4_BYTE_SHL2 = 0, 1
 MX_UNIT_FIXED8, MX_BLOCK32 = 0, 1
+DTYPE_F16, DTYPE_FP8, DTYPE_FP4, DTYPE_MXFP4 = 0, 1, 2, 3
+
+
+class Shard(ctypes.Structure):
+    """bw_shard_t: one GPU's part of a single-process sharded GEMM (include/bwgemm.h)."""
+
+    _fields_ = [("device", ctypes.c_int), ("A", ctypes.c_void_p), ("B", ctypes.c_void_p),
+                ("sfA", ctypes.c_void_p), ("sfB", ctypes.c_void_p), ("scale_a", ctypes.c_void_p),
+                ("scale_b", ctypes.c_void_p), ("C", ctypes.c_void_p), ("C_gathered", ctypes.c_void_p),
+                ("stream", ctypes.c_void_p)]
 
 
 class BwError(RuntimeError):
@@ -79,6 +89,7 @@ def lib():
         "bw_quantize_fp4": [P, P, P, I, I, I, I, I, P],
         "bw_quantize_mxfp4": [P, P, P, I, I, I, I, P],
         "bw_unshard_columns": [P, P, I, I, I, P],
+        "bw_gemm_sharded": [I, I, P, I, I, I, I, I],
     }
     for name, args in sig.items():
         f = getattr(L, name)
@@ -269,3 +280,24 @@ def unshard_columns(C_shardmajor, M: int, N: int, world: int, out=None, stream=N
         out = torch.empty((M, N), dtype=torch.float32, device=C_shardmajor.device)
     _check(lib().bw_unshard_columns(_ptr(C_shardmajor), _ptr(out), M, N, world, _stream(stream)))
     return out
+
+
+def gemm_sharded(dtype: int, parts: list[dict], M: int, N: int, K: int, out_dtype: int = OUT_F32,
+                 gather: bool = False) -> None:
+    """One process, len(parts) GPUs: parts[r] = {"A", "B", "C", optional "sfA", "sfB", "scale_a",
+    "scale_b", "C_gathered", "stream"} with torch tensors on the shard's device (B is the shard
+    of columns r*N/g .. (r+1)*N/g in the layout of the dtype's single-GPU call). Enqueues the
+    shards' GEMMs and, with gather, the NCCL all-gather + unshard into every C_gathered."""
+    import torch
+
+    arr = (Shard * max(1, len(parts)))()
+    for r, part in enumerate(parts):
+        dev = part["C"].device.index if part.get("C") is not None else 0
+        st = part.get("stream")
+        if st is None:
+            st = torch.cuda.current_stream(dev)
+        arr[r] = Shard(dev, _ptr(part.get("A")), _ptr(part.get("B")), _ptr(part.get("sfA")), _ptr(part.get("sfB")),
+                       _ptr(part.get("scale_a")), _ptr(part.get("scale_b")), _ptr(part.get("C")),
+                       _ptr(part.get("C_gathered")), _stream(st))
+    _check(lib().bw_gemm_sharded(dtype, out_dtype, ctypes.cast(arr, ctypes.c_void_p) if parts else None,
+                                 len(parts), M, N, K, int(gather)))

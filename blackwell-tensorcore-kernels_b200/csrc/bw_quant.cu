@@ -200,7 +200,8 @@ __global__ void k_quant_mx(const float* __restrict__ src, uint8_t* __restrict__ 
   }
 }
 
-__global__ void k_unshard(const float* __restrict__ src, float* __restrict__ dst, int M, int N, int world) {
+template <typename T>
+__global__ void k_unshard(const T* __restrict__ src, T* __restrict__ dst, int M, int N, int world) {
   const int ns = N / world;
   const long long total = static_cast<long long>(M) * N;
   const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
@@ -327,13 +328,30 @@ int bw_unshard_columns(const float* C_shardmajor, float* C_rowmajor, int M, int 
   DeviceState* d;
   int r = ensure_device(&d);
   if (r != BW_OK) return r;
-  k_unshard<<<grid_for(static_cast<long long>(M) * N, *d), kQThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+  k_unshard<float><<<grid_for(static_cast<long long>(M) * N, *d), kQThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       C_shardmajor, C_rowmajor, M, N, world);
   BW_CUDA(cudaGetLastError());
   return BW_OK;
 }
 
 }  // extern "C"
+
+namespace bw {
+// [world][M][N/world] -> M x N for 4- or 2-byte elements (FP32 or BF16 C), on the current device.
+int unshard_elems(const void* src, void* dst, int M, int N, int world, int elem_bytes, cudaStream_t stream) {
+  if (elem_bytes == 4) return bw_unshard_columns(static_cast<const float*>(src), static_cast<float*>(dst), M, N, world, stream);
+  if (elem_bytes != 2) return set_error(BW_ERR_INVALID, "unshard: element size %d", elem_bytes);
+  if (M < 0 || N < 0 || world <= 0 || N % world != 0) return set_error(BW_ERR_INVALID, "bad unshard shape");
+  if (static_cast<long long>(M) * N == 0) return BW_OK;
+  DeviceState* d;
+  int r = ensure_device(&d);
+  if (r != BW_OK) return r;
+  k_unshard<uint16_t><<<grid_for(static_cast<long long>(M) * N, *d), kQThreads, 0, stream>>>(
+      static_cast<const uint16_t*>(src), static_cast<uint16_t*>(dst), M, N, world);
+  BW_CUDA(cudaGetLastError());
+  return BW_OK;
+}
+}  // namespace bw
 
 // =========================================================================================
 // bw_quantize_fp8_noalloc: the per-tensor E4M3 quantiser for callers that cannot allocate

@@ -39,6 +39,9 @@ int make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, 
                  uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
                  CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B);
 
+// [world][M][N/world] -> row-major M x N for 4-byte (FP32) or 2-byte (BF16) elements.
+int unshard_elems(const void* src, void* dst, int M, int N, int world, int elem_bytes, cudaStream_t stream);
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace bw

@@ -155,6 +155,35 @@ size_t bw_sf_offset(int row, int kblock, int K);
  * [world][M][N/world]; this permutes it into row-major M x N. */
 int bw_unshard_columns(const float* C_shardmajor, float* C_rowmajor, int M, int N, int world, void* stream);
 
+/* One process driving g GPUs of a node (the single-process form of the sharded run).
+ * Shard r lives on `device` and holds the full A plus columns [r*N/g, (r+1)*N/g) of B in the
+ * layout the dtype's single-GPU entry point takes:
+ *   BW_DTYPE_F16    A M x K FP16, B K x (N/g) FP16 row-major; C FP32 (out_dtype BW_OUT_F32)
+ *   BW_DTYPE_FP8    A M x K E4M3, Bt (N/g) x K E4M3, optional device scales; C FP32 or BF16
+ *   BW_DTYPE_FP4    A, Bt packed E2M1 (K/2 bytes a row), optional device scales
+ *   BW_DTYPE_MXFP4  as FP4 plus the tiled UE8M0 scale factors of A and of the Bt shard
+ * C (M x N/g) is written on each device. With gather != 0 every C_gathered (M x N, row-major,
+ * on its shard's device) receives the whole product: an NCCL all-gather of the shards
+ * (ncclCommInitAll over the listed devices, cached; libnccl.so.2 is loaded on first use)
+ * followed by a column unshard. Work is enqueued on each shard's stream; the call does not
+ * synchronise. Replaces nothing in the reference (it runs on one GPU, src/main.cu:47-111).
+ * Returns BW_ERR_INVALID for bad arguments before touching any device, BW_ERR_UNSUPPORTED when
+ * a gather is requested and NCCL cannot be loaded. */
+enum { BW_DTYPE_F16 = 0, BW_DTYPE_FP8 = 1, BW_DTYPE_FP4 = 2, BW_DTYPE_MXFP4 = 3 };
+typedef struct {
+  int device;
+  const void* A;
+  const void* B;
+  const void* sfA;
+  const void* sfB;
+  const float* scale_a;
+  const float* scale_b;
+  void* C;
+  void* C_gathered;
+  void* stream;
+} bw_shard_t;
+int bw_gemm_sharded(int dtype, int out_dtype, const bw_shard_t* shards, int ngpu, int M, int N, int K, int gather);
+
 #ifdef __cplusplus
 }
 #endif

@@ -13,7 +13,7 @@ def test_header_declares_the_expected_surface():
     for must in ["bw_init", "bw_gemm_f16", "bw_gemm_f16_bt", "bw_gemm_fp8", "bw_gemm_mxfp4", "bw_gemm_fp4",
                  "bw_quantize_f16", "bw_quantize_fp8", "bw_quantize_fp4", "bw_quantize_mxfp4",
                  "bw_last_error_string", "bw_device_status", "bw_sf_bytes", "bw_sf_offset",
-                 "bw_unshard_columns"]:
+                 "bw_unshard_columns", "bw_gemm_sharded"]:
         assert must in names, must
 
 
@@ -48,3 +48,30 @@ def test_sf_layout_functions_match_oracle():
         for r in range(0, outer, 37):
             for j in range(K // 32):
                 assert bwgemm.lib().bw_sf_offset(r, j, K) == o.sf_offset(r, j, K)
+
+
+def test_sharded_argument_validation_without_gpu():
+    L = bwgemm.lib()
+    S = bwgemm.Shard
+    buf = ctypes.create_string_buffer(256)
+    p = (ctypes.addressof(buf) + 15) & ~15
+
+    def call(dtype, out, parts, M, N, K, gather):
+        arr = (S * max(1, len(parts)))(*parts)
+        return L.bw_gemm_sharded(dtype, out, ctypes.cast(arr, ctypes.c_void_p), len(parts), M, N, K, gather)
+
+    ok = S(0, p, p, None, None, None, None, p, None, None)
+    assert call(7, 0, [ok], 8, 8, 8, 0) == bwgemm.BW_ERR_INVALID                      # dtype
+    assert call(bwgemm.DTYPE_F16, bwgemm.OUT_BF16, [ok], 8, 8, 8, 0) == bwgemm.BW_ERR_INVALID  # FP16 writes FP32
+    assert L.bw_gemm_sharded(0, 0, None, 1, 8, 8, 8, 0) == bwgemm.BW_ERR_INVALID    # no shards
+    assert call(0, 0, [], 8, 8, 8, 0) == bwgemm.BW_ERR_INVALID                      # ngpu = 0
+    two = [S(0, p, p, None, None, None, None, p, None, None), S(1, p, p, None, None, None, None, p, None, None)]
+    assert call(0, 0, two, 8, 9, 8, 0) == bwgemm.BW_ERR_INVALID                     # N % ngpu
+    assert b"divisible" in L.bw_last_error_string()
+    dup = [S(0, p, p, None, None, None, None, p, None, None)] * 2
+    assert call(0, 0, dup, 8, 8, 8, 0) == bwgemm.BW_ERR_INVALID                     # same device twice
+    assert call(0, 0, two, 8, 8, 8, 1) == bwgemm.BW_ERR_INVALID                     # gather, no C_gathered
+    assert call(bwgemm.DTYPE_MXFP4, 1, two, 8, 8, 64, 0) == bwgemm.BW_ERR_INVALID   # MXFP4 without sfA/sfB
+    assert b"sfA" in L.bw_last_error_string()
+    nul = [S(0, None, p, None, None, None, None, p, None, None)]
+    assert call(0, 0, nul, 8, 8, 8, 0) == bwgemm.BW_ERR_INVALID                     # A null
