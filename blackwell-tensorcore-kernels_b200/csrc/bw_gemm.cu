@@ -158,7 +158,9 @@ GemmParams base_params(const DeviceState& d, void* C, int M, int N, int K) {
   p.K = K;
   p.ldc = N;
   p.group_m = env_int("BW_GROUP_M", 16);
-  p.hints = env_int("BW_L2_HINTS", 1);
+  // bit 0: A and B tiles evict-last in L2 (re-read by neighbouring tiles); bit 2: B evict-first
+  // instead, for M <= 256 where each B tile is read by one tile row (at most two)
+  p.hints = env_int("BW_L2_HINTS", M <= 256 ? 5 : 1);
   p.splits = 1;
   p.kb_per_split = 0;
   if (p.group_m < 1) p.group_m = 1;
@@ -181,10 +183,13 @@ int check_common(const void* A, const void* B, const void* C, int M, int N, int 
 // 128 x 256 single-CTA tiles split along K until there are >= 4 work units per SM, each split
 // >= 8 k-slabs; partial tiles are added into C (zeroed first, in stream order) by the TMA
 // reduce-add store. FP32 output only. Returns the split count (1 = no split).
+// FP32 outputs add the partial tiles into C; BF16 outputs add them into an FP32 workspace that
+// one conversion pass turns into C (BW_SPLITK_BF16=0 keeps BF16 outputs unsplit).
 int choose_splits(int M, int N, int nk, int out_elem, const DeviceState& d) {
   const int forced = env_int("BW_SPLITK", -1);
   if (forced >= 1) return forced;
-  if (forced == 0 || out_elem != 4 || M > 256) return 1;
+  if (forced == 0 || M > 256) return 1;
+  if (out_elem != 4 && env_int("BW_SPLITK_BF16", 1) == 0) return 1;
   const long tiles = static_cast<long>((M + 127) / 128) * ((N + 255) / 256);
   int s = 1;
   while (s < 8 && tiles * s < 4L * d.sms && nk / (2 * s) >= 8) s *= 2;
@@ -198,6 +203,48 @@ bool use_narrow(int M, int N, const DeviceState& d) {
   if (forced == 256) return false;
   const long tiles256 = static_cast<long>((M + 127) / 128) * ((N + 255) / 256);
   return tiles256 < d.sms;
+}
+
+// C (BF16) = workspace (FP32; scales already applied by the split-K epilogue), 8 per thread.
+__global__ void k_f32_to_bf16(const float4* __restrict__ src, uint4* __restrict__ dst, long long n8) {
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n8; i += stride) {
+    const float4 a = src[2 * i], b = src[2 * i + 1];
+    __nv_bfloat162 h0 = __floats2bfloat162_rn(a.x, a.y), h1 = __floats2bfloat162_rn(a.z, a.w);
+    __nv_bfloat162 h2 = __floats2bfloat162_rn(b.x, b.y), h3 = __floats2bfloat162_rn(b.z, b.w);
+    dst[i] = make_uint4(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1),
+                        *reinterpret_cast<uint32_t*>(&h2), *reinterpret_cast<uint32_t*>(&h3));
+  }
+}
+
+// Split-K launch of the single-CTA 128 x 256 kernel: partial tiles are TMA-reduce-added into C
+// zeroed in stream order (FP32 C), or for BF16 C into a per-stream FP32 workspace that one
+// conversion pass turns into C. BW_ERR_UNSUPPORTED (BF16 only) when every workspace slot
+// belongs to another stream: the caller then runs unsplit.
+template <Kind KIND, bool B_MN>
+int launch_split(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, GemmParams p, void* C,
+                 int out_dtype, cudaStream_t s, DeviceState& d) {
+  const size_t mn = static_cast<size_t>(p.M) * p.N;
+  if (out_dtype == BW_OUT_F32) {
+    BW_CUDA(cudaMemsetAsync(C, 0, 4 * mn, s));
+    return launch<KIND, B_MN, 256, 4, 2, Out::F32>(ta, tb, tc, p, s, d);
+  }
+  float* ws = nullptr;
+  int r = splitk_workspace(d, s, 4 * mn, &ws);
+  if (r != BW_OK) return r;
+  CUtensorMap tw;
+  if ((r = make_c_map(&tw, ws, p.M, p.N, BW_OUT_F32)) != BW_OK) return r;
+  p.C = ws;
+  BW_CUDA(cudaMemsetAsync(ws, 0, 4 * mn, s));
+  if ((r = launch<KIND, B_MN, 256, 4, 2, Out::F32>(ta, tb, tw, p, s, d)) != BW_OK) return r;
+  const long long n8 = static_cast<long long>(mn / 8);  // N % 8 == 0
+  long long blocks = (n8 + 255) / 256;
+  if (blocks > 8LL * d.sms) blocks = 8LL * d.sms;
+  if (blocks < 1) blocks = 1;
+  k_f32_to_bf16<<<static_cast<int>(blocks), 256, 0, s>>>(reinterpret_cast<const float4*>(ws), static_cast<uint4*>(C),
+                                                          n8);
+  BW_CUDA(cudaGetLastError());
+  return BW_OK;
 }
 
 size_t out_elem_bytes(int out_dtype) { return out_dtype == BW_OUT_BF16 ? 2 : 4; }
@@ -240,9 +287,8 @@ int gemm_f16_impl(const void* A, const void* B, float* C, int M, int N, int K, c
   }
   if (splits > 1) {
     if ((r = set_splits(p, splits, (K + 63) / 64)) != BW_OK) return r;
-    BW_CUDA(cudaMemsetAsync(C, 0, sizeof(float) * size_t(M) * N, s));
-    if (b_mn) return launch<Kind::F16, true, 256, 4, 2, Out::F32>(ta, tb, tc, p, s, *d);
-    return launch<Kind::F16, false, 256, 4, 2, Out::F32>(ta, tb, tc, p, s, *d);
+    if (b_mn) return launch_split<Kind::F16, true>(ta, tb, tc, p, C, BW_OUT_F32, s, *d);
+    return launch_split<Kind::F16, false>(ta, tb, tc, p, C, BW_OUT_F32, s, *d);
   }
   if (b_mn) {
     if (narrow) return launch<Kind::F16, true, 128, 6, 2, Out::F32>(ta, tb, tc, p, s, *d);
@@ -283,10 +329,12 @@ int gemm_fp8_impl(const uint8_t* A, const uint8_t* Bt, const float* sa, const fl
     if (direct) return launch_pair<Kind::F8, false, 3, Out::BF16, true, 2>(ta, tb, tc, p, s, *d);
     return launch_pair<Kind::F8, false, 3, Out::BF16, false, 2>(ta, tb, tc, p, s, *d);
   }
-  if (splits > 1) {  // FP32 output only (choose_splits)
+  if (splits > 1) {
     if ((r = set_splits(p, splits, (K + 127) / 128)) != BW_OK) return r;
-    BW_CUDA(cudaMemsetAsync(C, 0, sizeof(float) * size_t(M) * N, s));
-    return launch<Kind::F8, false, 256, 4, 2, Out::F32>(ta, tb, tc, p, s, *d);
+    r = launch_split<Kind::F8, false>(ta, tb, tc, p, C, out_dtype, s, *d);
+    if (r != BW_ERR_UNSUPPORTED) return r;
+    p.splits = 1;  // BF16 C and no workspace slot for this stream: run unsplit
+    p.kb_per_split = 0;
   }
   if (out_dtype == BW_OUT_F32) {
     if (narrow) return launch<Kind::F8, false, 128, 6, 2, Out::F32>(ta, tb, tc, p, s, *d);

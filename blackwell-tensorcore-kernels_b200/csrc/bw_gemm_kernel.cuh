@@ -76,7 +76,8 @@ struct GemmParams {
   int group_m;                 // raster: tile rows per group
   int splits;                  // single-CTA kernel: K splits per tile (>1: partials are TMA-reduce-added into zeroed C)
   int kb_per_split;            // k-slabs per split
-  int hints;                   // bit 0: A/B loads evict_last (else evict_normal); bit 1: C stores evict_first
+  int hints;                   // bit 0: A/B loads evict_last (else evict_normal); bit 1: C stores evict_first;
+                               // bit 2: B loads evict_first (single-CTA kernel)
   int* status;                 // device status word
   unsigned long long* trace;   // optional per-CTA wait-time trace (kTraceWords per CTA), or null
   unsigned long long budget_ns;
@@ -282,7 +283,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       const uint64_t pol_a = (p.hints & 1) ? l2_policy_evict_last() : l2_policy_evict_normal();
-      const uint64_t pol_b = pol_a;
+      const uint64_t pol_b = (p.hints & 4) ? l2_policy_evict_first() : pol_a;  // streamed-once B
       int s = 0;
       uint32_t ph = 0;
       bool ok = true;

@@ -113,6 +113,27 @@ int ensure_device(DeviceState** out) {
   return BW_OK;
 }
 
+int splitk_workspace(DeviceState& d, cudaStream_t stream, size_t bytes, float** out) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  DeviceState::SplitWs* slot = nullptr;
+  for (auto& w : d.splitk)
+    if (w.buf && w.stream == static_cast<void*>(stream)) { slot = &w; break; }
+  if (!slot)
+    for (auto& w : d.splitk)
+      if (!w.buf) { slot = &w; break; }
+  if (!slot) return set_error(BW_ERR_UNSUPPORTED, "split-K workspaces of %d streams in use", DeviceState::kSplitWs);
+  if (slot->bytes < bytes) {
+    if (slot->buf) BW_CUDA(cudaFree(slot->buf));  // synchronising: no launch still uses it
+    slot->buf = nullptr;
+    slot->bytes = 0;
+    BW_CUDA(cudaMalloc(&slot->buf, bytes));
+    slot->bytes = bytes;
+    slot->stream = stream;
+  }
+  *out = slot->buf;
+  return BW_OK;
+}
+
 int make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner, uint64_t outer,
                  uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle) {
   int r = load_encode();
@@ -163,6 +184,7 @@ int bw_shutdown(void) {
     cudaSetDevice(i);
     cudaFree(d.status);
     cudaFree(d.workspace);
+    for (auto& w : d.splitk) cudaFree(w.buf);
     d = DeviceState{};
   }
   cudaSetDevice(cur);

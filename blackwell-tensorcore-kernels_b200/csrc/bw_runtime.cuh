@@ -27,11 +27,21 @@ struct DeviceState {
   int* status = nullptr;         // device status word (kernels' bounded waits report here)
   void* workspace = nullptr;     // small scratch for quantiser reductions
   size_t workspace_bytes = 0;
+  struct SplitWs {               // FP32 split-K partial sums for BF16 outputs, one per stream
+    void* stream = nullptr;
+    float* buf = nullptr;
+    size_t bytes = 0;
+  };
+  static constexpr int kSplitWs = 8;
+  SplitWs splitk[kSplitWs];
 };
 
 // Ensures the current device is initialised; returns BW_OK or an error status.
 int ensure_device(DeviceState** out);
 unsigned long long wait_budget_ns();
+// FP32 workspace of at least `bytes` private to `stream` on this device (grown on demand, kept
+// until bw_shutdown); BW_ERR_UNSUPPORTED when every slot belongs to another stream.
+int splitk_workspace(DeviceState& d, cudaStream_t stream, size_t bytes, float** out);
 unsigned long long* trace_buffer(int ctas_needed);  // null unless bw_set_trace_buffer armed one
 
 // 2-D row-major tensor map: dims {inner, outer}, box {box_inner, box_outer}, 128B swizzle.

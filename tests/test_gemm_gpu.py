@@ -333,11 +333,12 @@ def test_fp4_pair_kernel_parity(cuda_dev, monkeypatch, M, N, K, out):
 
 
 @pytest.mark.parametrize("M,N,K", [(128, 4096, 1024), (77, 2056, 528), (200, 1024, 4096), (1, 1024, 1024)])
-@pytest.mark.parametrize("kind", ["f16", "fp8"])
+@pytest.mark.parametrize("kind", ["f16", "fp8", "fp8_bf16"])
 @pytest.mark.parametrize("splits", ["2", "3", "8"])
 def test_splitk_parity(cuda_dev, monkeypatch, M, N, K, kind, splits):
-    """Split-K (partial tiles TMA-reduce-added into zeroed C), forced with BW_SPLITK; uneven
-    k-slab ranges and more splits than k-slabs included."""
+    """Split-K (partial tiles TMA-reduce-added into zeroed C, or for BF16 C into an FP32
+    workspace converted afterwards), forced with BW_SPLITK; uneven k-slab ranges and more
+    splits than k-slabs included."""
     import torch
 
     monkeypatch.setenv("BW_SPLITK", splits)
@@ -354,14 +355,54 @@ def test_splitk_parity(cuda_dev, monkeypatch, M, N, K, kind, splits):
         B = o.seeded_normal((K, N), 94)
         qa, sa = bwgemm.quantize_fp8(_t(A, cuda_dev), False, bwgemm.SCALE_AMAX)
         qb, sb = bwgemm.quantize_fp8(_t(B, cuda_dev), True, bwgemm.SCALE_AMAX)
-        C = _np(bwgemm.gemm_fp8(qa, qb, sa, sb, out_dtype=bwgemm.OUT_F32))
+        bf16 = kind == "fp8_bf16"
+        C = _np(bwgemm.gemm_fp8(qa, qb, sa, sb, out_dtype=bwgemm.OUT_BF16 if bf16 else bwgemm.OUT_F32))
         ra, rsa = o.quant_fp8(A, False, o.SCALE_AMAX)
         rb, rsb = o.quant_fp8(B, True, o.SCALE_AMAX)
         R = o.gemm_f64(o.dequant_fp8(ra), o.dequant_fp8(rb), b_trans=True) * float(np.float32(rsa) * np.float32(rsb))
-        tol = o.lowp_tolerance(K, 448 * rsa, 448 * rsb)
+        tol = o.lowp_tolerance(K, 448 * rsa, 448 * rsb, np.abs(R).max(), bf16)
     torch.cuda.synchronize()
     _status_ok()
     assert np.abs(C - R).max() <= tol
+
+
+def test_splitk_bf16_workspace_per_stream(cuda_dev):
+    """Two streams running split-K BF16 GEMMs at once use separate FP32 workspaces; a larger
+    problem afterwards grows the workspace."""
+    import torch
+
+    outs, refs = [], []
+    streams = [torch.cuda.Stream(cuda_dev), torch.cuda.Stream(cuda_dev)]
+    for i, (M, N, K) in enumerate([(128, 8192, 4096), (64, 4096, 8192)]):
+        A = o.seeded_normal((M, K), 121 + i)
+        B = o.seeded_normal((K, N), 131 + i)
+        qa, sa = bwgemm.quantize_fp8(_t(A, cuda_dev), False, bwgemm.SCALE_AMAX)
+        qb, sb = bwgemm.quantize_fp8(_t(B, cuda_dev), True, bwgemm.SCALE_AMAX)
+        torch.cuda.synchronize()
+        ra, rsa = o.quant_fp8(A, False, o.SCALE_AMAX)
+        rb, rsb = o.quant_fp8(B, True, o.SCALE_AMAX)
+        R = o.gemm_f64(o.dequant_fp8(ra), o.dequant_fp8(rb), b_trans=True) * float(np.float32(rsa) * np.float32(rsb))
+        refs.append((R, o.lowp_tolerance(K, 448 * rsa, 448 * rsb, np.abs(R).max(), True)))
+        outs.append((qa, qb, sa, sb))
+    Cs = []
+    for _ in range(3):
+        Cs = [bwgemm.gemm_fp8(*outs[i], out_dtype=bwgemm.OUT_BF16, stream=streams[i]) for i in range(2)]
+    torch.cuda.synchronize()
+    _status_ok()
+    for C, (R, tol) in zip(Cs, refs):
+        assert np.abs(_np(C) - R).max() <= tol
+    # growth: a wider problem on the first stream
+    M, N, K = 256, 16384, 2048
+    A = o.seeded_normal((M, K), 141)
+    B = o.seeded_normal((K, N), 142)
+    qa, sa = bwgemm.quantize_fp8(_t(A, cuda_dev), False, bwgemm.SCALE_AMAX)
+    qb, sb = bwgemm.quantize_fp8(_t(B, cuda_dev), True, bwgemm.SCALE_AMAX)
+    C = bwgemm.gemm_fp8(qa, qb, sa, sb, out_dtype=bwgemm.OUT_BF16, stream=streams[0])
+    torch.cuda.synchronize()
+    ra, rsa = o.quant_fp8(A, False, o.SCALE_AMAX)
+    rb, rsb = o.quant_fp8(B, True, o.SCALE_AMAX)
+    R = o.gemm_f64(o.dequant_fp8(ra), o.dequant_fp8(rb), b_trans=True) * float(np.float32(rsa) * np.float32(rsb))
+    assert np.abs(_np(C) - R).max() <= o.lowp_tolerance(K, 448 * rsa, 448 * rsb, np.abs(R).max(), True)
 
 
 @pytest.mark.parametrize("N", [520, 1032])
