@@ -89,6 +89,7 @@ def lib():
         "bw_quantize_fp4": [P, P, P, I, I, I, I, I, P],
         "bw_quantize_mxfp4": [P, P, P, I, I, I, I, P],
         "bw_unshard_columns": [P, P, I, I, I, P],
+        "bw_unshard_columns_bf16": [P, P, I, I, I, P],
         "bw_gemm_sharded": [I, I, P, I, I, I, I, I],
     }
     for name, args in sig.items():
@@ -274,11 +275,19 @@ def quantize_mxfp4(src, transpose=False, mode=MX_BLOCK32, dst=None, sf=None, str
 
 
 def unshard_columns(C_shardmajor, M: int, N: int, world: int, out=None, stream=None):
+    """[world][M][N/world] -> row-major M x N on the device; FP32 or BF16 elements."""
     import torch
 
+    if C_shardmajor.dtype not in (torch.float32, torch.bfloat16):
+        raise TypeError(f"unshard_columns takes float32 or bfloat16, not {C_shardmajor.dtype}")
+    if C_shardmajor.numel() != M * N:
+        raise ValueError(f"shard-major buffer holds {C_shardmajor.numel()} elements, expected {M} x {N}")
     if out is None:
-        out = torch.empty((M, N), dtype=torch.float32, device=C_shardmajor.device)
-    _check(lib().bw_unshard_columns(_ptr(C_shardmajor), _ptr(out), M, N, world, _stream(stream)))
+        out = torch.empty((M, N), dtype=C_shardmajor.dtype, device=C_shardmajor.device)
+    if out.dtype != C_shardmajor.dtype or out.numel() != M * N:
+        raise ValueError("out must match the input's dtype and hold M x N elements")
+    fn = lib().bw_unshard_columns if C_shardmajor.dtype == torch.float32 else lib().bw_unshard_columns_bf16
+    _check(fn(_ptr(C_shardmajor), _ptr(out), M, N, world, _stream(stream)))
     return out
 
 

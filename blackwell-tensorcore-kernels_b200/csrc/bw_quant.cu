@@ -334,6 +334,13 @@ int bw_unshard_columns(const float* C_shardmajor, float* C_rowmajor, int M, int 
   return BW_OK;
 }
 
+int bw_unshard_columns_bf16(const void* C_shardmajor, void* C_rowmajor, int M, int N, int world, void* stream) {
+  if (M < 0 || N < 0 || world <= 0 || N % world != 0) return set_error(BW_ERR_INVALID, "bad unshard shape");
+  if (static_cast<long long>(M) * N == 0) return BW_OK;
+  if (!C_shardmajor || !C_rowmajor) return set_error(BW_ERR_INVALID, "null buffer");
+  return unshard_elems(C_shardmajor, C_rowmajor, M, N, world, 2, static_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"
 
 namespace bw {

@@ -154,6 +154,8 @@ size_t bw_sf_offset(int row, int kblock, int K);
  * all-gathers the M x (N/world) shards over NCCL, which yields a shard-major buffer
  * [world][M][N/world]; this permutes it into row-major M x N. */
 int bw_unshard_columns(const float* C_shardmajor, float* C_rowmajor, int M, int N, int world, void* stream);
+/* The same permutation for 2-byte elements (BF16 C). */
+int bw_unshard_columns_bf16(const void* C_shardmajor, void* C_rowmajor, int M, int N, int world, void* stream);
 
 /* One process driving g GPUs of a node (the single-process form of the sharded run).
  * Shard r lives on `device` and holds the full A plus columns [r*N/g, (r+1)*N/g) of B in the

@@ -242,15 +242,21 @@ def test_fp4_per_tensor_parity(cuda_dev, M, N, K):
     assert err <= tol, (err, tol)
 
 
-def test_unshard_columns(cuda_dev):
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16"])
+def test_unshard_columns(cuda_dev, dtype):
+    """Both element sizes; a BF16 buffer must not be walked as FP32 (that read past its end)."""
     import torch
 
     M, N, world = 64, 96, 4
     full = o.seeded_uniform((M, N), 9)
     shards = np.stack([full[:, r * (N // world):(r + 1) * (N // world)] for r in range(world)])
-    out = bwgemm.unshard_columns(_t(np.ascontiguousarray(shards), cuda_dev), M, N, world)
+    src = _t(np.ascontiguousarray(shards), cuda_dev).to(getattr(torch, dtype))
+    out = bwgemm.unshard_columns(src, M, N, world)
     torch.cuda.synchronize()
-    assert np.array_equal(_np(out), full)
+    assert out.dtype == src.dtype
+    assert torch.equal(out.cpu(), torch.from_numpy(full).to(src.dtype))
+    with pytest.raises(ValueError):
+        bwgemm.unshard_columns(src, M, N + world, world)
 
 
 @pytest.mark.parametrize("kind", ["f16", "fp8"])
