@@ -213,12 +213,47 @@ __global__ void k_unshard(const T* __restrict__ src, T* __restrict__ dst, int M,
   }
 }
 
+// Same permutation, 16 bytes per thread: blockIdx.y walks rows, x walks 16-byte column
+// groups (a group never straddles two shards when a shard row is a multiple of 16 bytes).
+template <typename T>
+__global__ void k_unshard_vec(const T* __restrict__ src, T* __restrict__ dst, int M, int N, int world) {
+  constexpr int V = 16 / sizeof(T);
+  const int ns = N / world;
+  const int groups = N / V;
+  for (int m = blockIdx.y; m < M; m += gridDim.y) {
+    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < groups; j += gridDim.x * blockDim.x) {
+      const int c = j * V;
+      const int r = c / ns, cc = c - r * ns;
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(src + (static_cast<size_t>(r) * M + m) * ns + cc));
+      *reinterpret_cast<uint4*>(dst + static_cast<size_t>(m) * N + c) = v;
+    }
+  }
+}
+
+template <typename T>
+int launch_unshard(const T* src, T* dst, int M, int N, int world, cudaStream_t s, const DeviceState& d);
+
 int grid_for(long long n, const DeviceState& d) {
   long long g = (n + kQThreads - 1) / kQThreads;
   const long long cap = static_cast<long long>(d.sms) * 16;
   if (g > cap) g = cap;
   if (g < 1) g = 1;
   return static_cast<int>(g);
+}
+
+template <typename T>
+int launch_unshard(const T* src, T* dst, int M, int N, int world, cudaStream_t s, const DeviceState& d) {
+  const int ns = N / world;
+  const bool vec = (ns * sizeof(T)) % 16 == 0 && ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15u) == 0;
+  if (vec) {
+    const int groups = N / static_cast<int>(16 / sizeof(T));
+    dim3 grid((groups + 255) / 256, M < 65535 ? M : 65535);
+    k_unshard_vec<T><<<grid, 256, 0, s>>>(src, dst, M, N, world);
+  } else {
+    k_unshard<T><<<grid_for(static_cast<long long>(M) * N, d), kQThreads, 0, s>>>(src, dst, M, N, world);
+  }
+  BW_CUDA(cudaGetLastError());
+  return BW_OK;
 }
 
 // Shared driver for the per-tensor quantisers (fp8 and fp4).
@@ -328,10 +363,7 @@ int bw_unshard_columns(const float* C_shardmajor, float* C_rowmajor, int M, int 
   DeviceState* d;
   int r = ensure_device(&d);
   if (r != BW_OK) return r;
-  k_unshard<float><<<grid_for(static_cast<long long>(M) * N, *d), kQThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      C_shardmajor, C_rowmajor, M, N, world);
-  BW_CUDA(cudaGetLastError());
-  return BW_OK;
+  return launch_unshard<float>(C_shardmajor, C_rowmajor, M, N, world, static_cast<cudaStream_t>(stream), *d);
 }
 
 int bw_unshard_columns_bf16(const void* C_shardmajor, void* C_rowmajor, int M, int N, int world, void* stream) {
@@ -353,10 +385,7 @@ int unshard_elems(const void* src, void* dst, int M, int N, int world, int elem_
   DeviceState* d;
   int r = ensure_device(&d);
   if (r != BW_OK) return r;
-  k_unshard<uint16_t><<<grid_for(static_cast<long long>(M) * N, *d), kQThreads, 0, stream>>>(
-      static_cast<const uint16_t*>(src), static_cast<uint16_t*>(dst), M, N, world);
-  BW_CUDA(cudaGetLastError());
-  return BW_OK;
+  return launch_unshard<uint16_t>(static_cast<const uint16_t*>(src), static_cast<uint16_t*>(dst), M, N, world, stream, *d);
 }
 }  // namespace bw
 

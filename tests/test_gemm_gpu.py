@@ -243,11 +243,12 @@ def test_fp4_per_tensor_parity(cuda_dev, M, N, K):
 
 
 @pytest.mark.parametrize("dtype", ["float32", "bfloat16"])
-def test_unshard_columns(cuda_dev, dtype):
-    """Both element sizes; a BF16 buffer must not be walked as FP32 (that read past its end)."""
+@pytest.mark.parametrize("M,N,world", [(64, 96, 4), (33, 72, 4), (5, 4096, 8)])
+def test_unshard_columns(cuda_dev, dtype, M, N, world):
+    """Both element sizes, 16-byte and scalar paths (72 / 4 columns per shard is not a whole
+    number of 16-byte groups); a BF16 buffer must not be walked as FP32 (that read past its end)."""
     import torch
 
-    M, N, world = 64, 96, 4
     full = o.seeded_uniform((M, N), 9)
     shards = np.stack([full[:, r * (N // world):(r + 1) * (N // world)] for r in range(world)])
     src = _t(np.ascontiguousarray(shards), cuda_dev).to(getattr(torch, dtype))
