@@ -12,6 +12,7 @@
 #include <cuda_fp16.h>
 #include <cuda_fp8.h>
 
+#include "bw_e2m1.h"
 #include "bw_runtime.cuh"
 
 namespace bw {
@@ -19,18 +20,7 @@ namespace {
 
 constexpr int kQThreads = 256;
 
-__device__ __forceinline__ uint8_t e2m1_code(float v) {
-  const float lv[8] = {0.f, 0.5f, 1.f, 1.5f, 2.f, 3.f, 4.f, 6.f};
-  const float a = fabsf(v);
-  int best = 0;
-  float bd = fabsf(a - lv[0]);
-#pragma unroll
-  for (int i = 1; i < 8; ++i) {
-    const float d = fabsf(a - lv[i]);
-    if (d < bd) { bd = d; best = i; }
-  }
-  return static_cast<uint8_t>((v < 0.f ? 8 : 0) | best);
-}
+__device__ __forceinline__ uint8_t e2m1_code(float v) { return bw_e2m1_code(v); }
 
 __device__ __forceinline__ uint8_t e4m3_sat(float x) {
   return static_cast<uint8_t>(__nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3));
@@ -56,8 +46,17 @@ __global__ void k_f32_to_f16(const float* __restrict__ src, __half* __restrict__
 __global__ void k_amax(const float* __restrict__ src, long long n, unsigned* __restrict__ out) {
   float m = 0.f;
   const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
-  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n; i += stride)
-    m = fmaxf(m, fabsf(src[i]));
+  const long long t0 = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  if ((reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
+    const long long n4 = n / 4;
+    for (long long i = t0; i < n4; i += stride) {
+      const float4 f = __ldg(reinterpret_cast<const float4*>(src) + i);
+      m = fmaxf(m, fmaxf(fmaxf(fabsf(f.x), fabsf(f.y)), fmaxf(fabsf(f.z), fabsf(f.w))));
+    }
+    for (long long i = 4 * n4 + t0; i < n; i += stride) m = fmaxf(m, fabsf(src[i]));
+  } else {
+    for (long long i = t0; i < n; i += stride) m = fmaxf(m, fabsf(src[i]));
+  }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
   __shared__ float wm[kQThreads / 32];
@@ -85,13 +84,39 @@ __device__ __forceinline__ void tensor_scale(int mode, const unsigned* amax_bits
 
 // Quantise rows x cols fp32 into dst (rows x cols, or cols x rows when transposing).
 // FMT 0 = e4m3 byte, 1 = e2m1 byte container (<<2), 2 = e2m1 packed pairs.
-// Transposes go through a 32 x 33 shared tile so both sides stay coalesced.
 template <int FMT>
 __device__ __forceinline__ uint8_t encode(float x) {
   if constexpr (FMT == 0) return e4m3_sat(x);
   else return e2m1_code(x);
 }
 
+template <int FMT>
+__device__ __forceinline__ uint32_t encode_byte(float x) {
+  const uint32_t c = encode<FMT>(x);
+  return FMT == 1 ? (c << 2) : c;
+}
+
+// 16 consecutive values -> 16 code bytes (FMT 0/1) or 8 packed bytes (FMT 2).
+template <int FMT>
+__device__ __forceinline__ void encode16(const float (&v)[16], float mul, uint32_t (&w)[4]) {
+  if constexpr (FMT == 2) {
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      w[q] = 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) w[q] |= static_cast<uint32_t>(e2m1_code(v[8 * q + i] * mul)) << (4 * i);
+    }
+    w[2] = w[3] = 0;
+  } else {
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      w[q] = encode_byte<FMT>(v[4 * q] * mul) | (encode_byte<FMT>(v[4 * q + 1] * mul) << 8) |
+             (encode_byte<FMT>(v[4 * q + 2] * mul) << 16) | (encode_byte<FMT>(v[4 * q + 3] * mul) << 24);
+  }
+}
+
+// Row-major output: 16 elements per thread per step (four float4 loads, one 16- or 8-byte
+// store) when src/dst alignment and n allow it; element-wise otherwise.
 template <int FMT>
 __global__ void k_quant_rowmajor(const float* __restrict__ src, uint8_t* __restrict__ dst, int rows, int cols,
                                  int mode, float qmax, const unsigned* amax_bits, float* scale_out) {
@@ -100,103 +125,178 @@ __global__ void k_quant_rowmajor(const float* __restrict__ src, uint8_t* __restr
   if (scale_out && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) *scale_out = s;
   const long long n = static_cast<long long>(rows) * cols;
   const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  const long long t0 = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  const bool vec = n % 16 == 0 && (reinterpret_cast<uintptr_t>(src) & 15u) == 0 &&
+                   (reinterpret_cast<uintptr_t>(dst) & (FMT == 2 ? 7u : 15u)) == 0;
+  if (vec) {
+    for (long long i = t0; i < n / 16; i += stride) {
+      float v[16];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 f = __ldcs(reinterpret_cast<const float4*>(src) + 4 * i + q);
+        v[4 * q] = f.x; v[4 * q + 1] = f.y; v[4 * q + 2] = f.z; v[4 * q + 3] = f.w;
+      }
+      uint32_t w[4];
+      encode16<FMT>(v, mul, w);
+      if constexpr (FMT == 2) reinterpret_cast<uint2*>(dst)[i] = make_uint2(w[0], w[1]);
+      else reinterpret_cast<uint4*>(dst)[i] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    return;
+  }
   if constexpr (FMT == 2) {
     const long long npairs = n / 2;  // cols is even: pairs never straddle rows
-    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < npairs; i += stride) {
+    for (long long i = t0; i < npairs; i += stride) {
       const float2 v = reinterpret_cast<const float2*>(src)[i];
       dst[i] = static_cast<uint8_t>(e2m1_code(v.x * mul) | (e2m1_code(v.y * mul) << 4));
     }
   } else {
-    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n; i += stride) {
-      const uint8_t c = encode<FMT>(src[i] * mul);
-      dst[i] = (FMT == 1) ? static_cast<uint8_t>(c << 2) : c;
-    }
+    for (long long i = t0; i < n; i += stride) dst[i] = static_cast<uint8_t>(encode_byte<FMT>(src[i] * mul));
   }
 }
 
+// src rows x cols -> dst cols x rows. A CTA takes 128 src rows x 32 src columns: lane = column,
+// warp w = rows r0 + 16w .. +15 (16 coalesced 128-byte row loads), so each thread ends with 16
+// consecutive codes of one dst row and stores them as one 16-byte (8 packed bytes for FMT 2)
+// store when rows % 16 == 0 and dst is aligned; byte stores otherwise.
+constexpr int kQuantColsRows = 128;
 template <int FMT>
-__global__ void k_quant_transpose(const float* __restrict__ src, uint8_t* __restrict__ dst, int rows, int cols,
-                                  int mode, float qmax, const unsigned* amax_bits, float* scale_out) {
-  // src rows x cols -> dst cols x rows. Block handles a 64 (src rows) x 32 (src cols) tile.
-  __shared__ float tile[64][33];
+__global__ void __launch_bounds__(256) k_quant_transpose(const float* __restrict__ src, uint8_t* __restrict__ dst,
+                                                         int rows, int cols, int mode, float qmax,
+                                                         const unsigned* amax_bits, float* scale_out) {
   float mul, s;
   tensor_scale(mode, amax_bits, qmax, mul, s);
   if (scale_out && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) *scale_out = s;
-  const int r0 = blockIdx.y * 64, c0 = blockIdx.x * 32;
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
-  for (int i = ty; i < 64; i += 8) {
-    const int r = r0 + i, c = c0 + tx;
-    tile[i][tx] = (r < rows && c < cols) ? src[static_cast<size_t>(r) * cols + c] * mul : 0.f;
-  }
-  __syncthreads();
+  const int c = blockIdx.x * 32 + (threadIdx.x & 31);
+  const int r0 = blockIdx.y * kQuantColsRows + 16 * (threadIdx.x >> 5);
+  if (c >= cols || r0 >= rows) return;
+  float v[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = (r0 + i < rows) ? __ldcs(src + static_cast<size_t>(r0 + i) * cols + c) : 0.f;
+  const bool vec = rows % 16 == 0 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0;
+  uint32_t w[4];
+  encode16<FMT>(v, mul, w);
   if constexpr (FMT == 2) {
-    // dst row = src column c0 + j; 64 src rows -> 32 packed bytes per dst row.
-    for (int j = ty; j < 32; j += 8) {
-      const int c = c0 + j, r = r0 + 2 * tx;
-      if (c < cols && r < rows)
-        dst[static_cast<size_t>(c) * (rows / 2) + r / 2] =
-            static_cast<uint8_t>(e2m1_code(tile[2 * tx][j]) | (e2m1_code(tile[2 * tx + 1][j]) << 4));
+    uint8_t* row = dst + static_cast<size_t>(c) * (rows / 2);
+    if (vec) {
+      *reinterpret_cast<uint2*>(row + r0 / 2) = make_uint2(w[0], w[1]);
+    } else {
+      for (int i = 0; i < 16 && r0 + i < rows; i += 2) row[(r0 + i) / 2] = static_cast<uint8_t>(w[i / 8] >> (4 * (i % 8)));
     }
   } else {
-    for (int j = ty; j < 32; j += 8) {
-      const int c = c0 + j;
-      for (int h = 0; h < 2; ++h) {
-        const int i = tx + 32 * h, r = r0 + i;
-        if (c < cols && r < rows) {
-          const uint8_t code = encode<FMT>(tile[i][j]);
-          dst[static_cast<size_t>(c) * rows + r] = (FMT == 1) ? static_cast<uint8_t>(code << 2) : code;
-        }
-      }
+    uint8_t* row = dst + static_cast<size_t>(c) * rows;
+    if (vec) {
+      *reinterpret_cast<uint4*>(row + r0) = make_uint4(w[0], w[1], w[2], w[3]);
+    } else {
+      for (int i = 0; i < 16 && r0 + i < rows; ++i) row[r0 + i] = static_cast<uint8_t>(w[i / 4] >> (8 * (i % 4)));
     }
   }
 }
 
-// MXFP4: one thread per (outer index o, 32-element K block j).
-__global__ void k_quant_mx(const float* __restrict__ src, uint8_t* __restrict__ dst, uint8_t* __restrict__ sf,
-                           int outer, int K, int transpose, int src_cols, int mode) {
+// MXFP4 block scale: e = floor(log2(block amax)) - 2 read from the exponent field; zero and
+// subnormal blocks clamp to e = -127 (byte 0). Returns the UE8M0 byte and the multiplier 2^-e.
+__device__ __forceinline__ uint8_t mx_block_scale(float amax, int mode, float& mul) {
+  if (mode != BW_MX_BLOCK32) {
+    mul = 8.f;
+    return 127;
+  }
+  const int biased = static_cast<int>((__float_as_uint(amax) >> 23) & 0xFF);
+  int e = (biased == 0) ? -127 : biased - 127 - 2;
+  if (e < -127) e = -127;
+  if (e > 127) e = 127;
+  const int mexp = 127 - e;  // exponent field of 2^-e, in [0, 254]
+  mul = (mexp >= 1) ? __uint_as_float(static_cast<uint32_t>(mexp) << 23) : 1.f;
+  if (e == -127) mul = __uint_as_float(254u << 23);  // 2^127
+  return static_cast<uint8_t>(e + 127);
+}
+
+__device__ __forceinline__ size_t sf_index(int o, int j, size_t kgroups) {
+  const int r = o % 128;
+  return ((static_cast<size_t>(o) / 128) * kgroups + j / 4) * 512 + (r % 32) * 16 + (r / 32) * 4 + (j % 4);
+}
+
+// MXFP4, K contiguous in src (outer x K row-major): one thread per 32-element block, eight
+// float4 loads and one 16-byte store of its packed codes (a warp stores 512 contiguous bytes:
+// the packed output is flat in the block index b = o * (K/32) + j). Measured faster than
+// warp-cooperative forms that share a block across lanes (fewer instructions per element).
+__global__ void __launch_bounds__(256) k_quant_mx_rows(const float4* __restrict__ src, uint4* __restrict__ dst,
+                                                        uint8_t* __restrict__ sf, int nkb, int nblocks, int mode) {
+  const unsigned kg = (static_cast<unsigned>(nkb) + 3u) / 4u;
+  for (int b = blockIdx.x * blockDim.x + threadIdx.x; b < nblocks; b += gridDim.x * blockDim.x) {
+    float4 x[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) x[i] = __ldcs(src + static_cast<size_t>(b) * 8 + i);
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      amax = fmaxf(amax, fmaxf(fmaxf(fabsf(x[i].x), fabsf(x[i].y)), fmaxf(fabsf(x[i].z), fabsf(x[i].w))));
+    float mul;
+    const uint8_t byte = mx_block_scale(amax, mode, mul);
+    uint32_t w[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float4 a = x[2 * q], c = x[2 * q + 1];
+      w[q] = static_cast<uint32_t>(e2m1_code(a.x * mul)) | (static_cast<uint32_t>(e2m1_code(a.y * mul)) << 4) |
+             (static_cast<uint32_t>(e2m1_code(a.z * mul)) << 8) | (static_cast<uint32_t>(e2m1_code(a.w * mul)) << 12) |
+             (static_cast<uint32_t>(e2m1_code(c.x * mul)) << 16) | (static_cast<uint32_t>(e2m1_code(c.y * mul)) << 20) |
+             (static_cast<uint32_t>(e2m1_code(c.z * mul)) << 24) | (static_cast<uint32_t>(e2m1_code(c.w * mul)) << 28);
+    }
+    dst[b] = make_uint4(w[0], w[1], w[2], w[3]);
+    const unsigned o = static_cast<unsigned>(b) / static_cast<unsigned>(nkb);
+    const unsigned j = static_cast<unsigned>(b) - o * static_cast<unsigned>(nkb);
+    const unsigned r = o & 127u;
+    sf[(static_cast<size_t>(o >> 7) * kg + (j >> 2)) * 512 + (r & 31u) * 16 + (r >> 5) * 4 + (j & 3u)] = byte;
+  }
+}
+
+// MXFP4 from a K x outer source (the Bt operand built from row-major B): a CTA takes 32
+// outer columns x 256 K. Warp w quantises K block w of the tile for 32 columns (lane = column,
+// 32 coalesced 128-byte row loads), the packed blocks and scale bytes go through shared memory,
+// and the tile leaves as 32 output rows x 128 contiguous bytes.
+__global__ void __launch_bounds__(256) k_quant_mx_cols(const float* __restrict__ src, uint8_t* __restrict__ dst,
+                                                       uint8_t* __restrict__ sf, int K, int outer, int mode) {
+  __shared__ uint4 packed[32][9];  // [column][K block], padded
+  __shared__ uint8_t scales[32][8];
+  const int lane = threadIdx.x & 31, wk = threadIdx.x >> 5;
+  const int o0 = blockIdx.x * 32, k0 = blockIdx.y * 256;
   const int nkb = K / 32;
-  const long long total = static_cast<long long>(outer) * nkb;
-  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
-  const size_t kg = (static_cast<size_t>(nkb) + 3) / 4;
-  for (long long t = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; t < total; t += stride) {
-    // Transposed sources put consecutive threads on consecutive o (coalesced along src rows).
-    const int o = transpose ? static_cast<int>(t % outer) : static_cast<int>(t / nkb);
-    const int j = transpose ? static_cast<int>(t / outer) : static_cast<int>(t % nkb);
+  const int j = k0 / 32 + wk;  // this warp's K block
+  const int o = o0 + lane;
+  if (j < nkb && o < outer) {
     float v[32];
-    if (transpose) {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] = src[static_cast<size_t>(j * 32 + i) * src_cols + o];
-    } else {
-      const float4* p4 = reinterpret_cast<const float4*>(src + static_cast<size_t>(o) * K + j * 32);
+    for (int i = 0; i < 32; ++i) v[i] = __ldg(src + static_cast<size_t>(j * 32 + i) * outer + o);
+    float amax = 0.f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float4 q = p4[i];
-        v[4 * i] = q.x; v[4 * i + 1] = q.y; v[4 * i + 2] = q.z; v[4 * i + 3] = q.w;
-      }
-    }
-    float mul = 8.f;
-    uint8_t byte = 127;
-    if (mode == BW_MX_BLOCK32) {
-      float amax = 0.f;
-#pragma unroll
-      for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
-      // e = floor(log2(amax)) - 2 read from the exponent field; zero and subnormal blocks
-      // clamp to e = -127 (byte 0). Multiplier 2^-e is built from its exponent bits.
-      const int biased = static_cast<int>((__float_as_uint(amax) >> 23) & 0xFF);
-      int e = (biased == 0) ? -127 : biased - 127 - 2;
-      if (e < -127) e = -127;
-      if (e > 127) e = 127;
-      byte = static_cast<uint8_t>(e + 127);
-      const int mexp = 127 - e;  // exponent field of 2^-e, in [0, 254]
-      mul = (mexp >= 1) ? __uint_as_float(static_cast<uint32_t>(mexp) << 23) : 1.f;
-      if (e == -127) mul = __uint_as_float(254u << 23);  // 2^127
-    }
+    for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    float mul;
+    scales[lane][wk] = mx_block_scale(amax, mode, mul);
     uint32_t w[4] = {0, 0, 0, 0};
 #pragma unroll
     for (int i = 0; i < 32; ++i) w[i / 8] |= static_cast<uint32_t>(e2m1_code(v[i] * mul)) << (4 * (i % 8));
-    *reinterpret_cast<uint4*>(dst + static_cast<size_t>(o) * (K / 2) + j * 16) = make_uint4(w[0], w[1], w[2], w[3]);
-    const int r = o % 128;
-    sf[((static_cast<size_t>(o) / 128) * kg + j / 4) * 512 + (r % 32) * 16 + (r / 32) * 4 + (j % 4)] = byte;
+    packed[lane][wk] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+  __syncthreads();
+  // 32 rows x 8 blocks of 16 bytes: thread t writes block t % 8 of row t / 8
+  {
+    const int r = threadIdx.x >> 3, c = threadIdx.x & 7;
+    const int oo = o0 + r, jj = k0 / 32 + c;
+    if (oo < outer && jj < nkb)
+      *reinterpret_cast<uint4*>(dst + static_cast<size_t>(oo) * (K / 2) + static_cast<size_t>(jj) * 16) = packed[r][c];
+  }
+  // scale bytes: 4 consecutive K blocks of one row are one aligned 32-bit word of the layout
+  if (threadIdx.x < 64) {
+    const int r = threadIdx.x >> 1, g = threadIdx.x & 1;
+    const int oo = o0 + r, jj = k0 / 32 + 4 * g;
+    const size_t kg = (static_cast<size_t>(nkb) + 3) / 4;
+    if (oo < outer && jj < nkb) {
+      if (jj + 3 < nkb) {
+        const uint32_t word = scales[r][4 * g] | (scales[r][4 * g + 1] << 8) | (scales[r][4 * g + 2] << 16) |
+                              (static_cast<uint32_t>(scales[r][4 * g + 3]) << 24);
+        *reinterpret_cast<uint32_t*>(sf + sf_index(oo, jj, kg)) = word;
+      } else {
+        for (int t = 0; t < 4 && jj + t < nkb; ++t) sf[sf_index(oo, jj + t, kg)] = scales[r][4 * g + t];
+      }
+    }
   }
 }
 
@@ -286,8 +386,8 @@ int quant_tensor(const float* src, uint8_t* dst, float* scale_out, int rows, int
     BW_CUDA(cudaGetLastError());
   }
   if (transpose) {
-    dim3 grid((cols + 31) / 32, (rows + 63) / 64);
-    k_quant_transpose<FMT><<<grid, kQThreads, 0, s>>>(src, dst, rows, cols, mode, qmax, amax, scale_out);
+    dim3 grid((cols + 31) / 32, (rows + kQuantColsRows - 1) / kQuantColsRows);
+    k_quant_transpose<FMT><<<grid, 256, 0, s>>>(src, dst, rows, cols, mode, qmax, amax, scale_out);
   } else {
     k_quant_rowmajor<FMT><<<grid_for(FMT == 2 ? n / 2 : n, *d), kQThreads, 0, s>>>(src, dst, rows, cols, mode, qmax,
                                                                                   amax, scale_out);
@@ -350,8 +450,17 @@ int bw_quantize_mxfp4(const float* src, uint8_t* dst, uint8_t* sf, int rows, int
   if (r != BW_OK) return r;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   BW_CUDA(cudaMemsetAsync(sf, 0x7f, bw_sf_bytes(outer, K), s));
-  const long long total = static_cast<long long>(outer) * (K / 32);
-  k_quant_mx<<<grid_for(total, *d), kQThreads, 0, s>>>(src, dst, sf, outer, K, transpose, cols, mode);
+  if (transpose) {
+    dim3 grid((outer + 31) / 32, (K + 255) / 256);
+    k_quant_mx_cols<<<grid, 256, 0, s>>>(src, dst, sf, K, outer, mode);
+  } else {
+    const long long nblocks = static_cast<long long>(outer) * (K / 32);
+    if (nblocks >= (1LL << 31) - 256) return set_error(BW_ERR_INVALID, "mxfp4: %lld blocks exceed the index range", nblocks);
+    const long long ctas = (nblocks + 255) / 256;
+    const long long cap = static_cast<long long>(d->sms) * 32;
+    k_quant_mx_rows<<<static_cast<int>(ctas < cap ? ctas : cap), 256, 0, s>>>(
+        reinterpret_cast<const float4*>(src), reinterpret_cast<uint4*>(dst), sf, K / 32, static_cast<int>(nblocks), mode);
+  }
   BW_CUDA(cudaGetLastError());
   return BW_OK;
 }
@@ -514,8 +623,8 @@ extern "C" int bw_quantize_fp8_noalloc(const float* src, uint8_t* dst, float* sc
     BW_CUDA(cudaGetLastError());
   }
   if (transpose) {
-    dim3 grid((cols + 31) / 32, (rows + 63) / 64);
-    k_quant_transpose<0><<<grid, kQThreads, 0, s>>>(src, dst, rows, cols, scale_mode, 448.f, amax, scale_out);
+    dim3 grid((cols + 31) / 32, (rows + kQuantColsRows - 1) / kQuantColsRows);
+    k_quant_transpose<0><<<grid, 256, 0, s>>>(src, dst, rows, cols, scale_mode, 448.f, amax, scale_out);
   } else {
     long long g = (n + kQThreads - 1) / kQThreads;
     if (g > static_cast<long long>(sms) * 16) g = static_cast<long long>(sms) * 16;

@@ -142,8 +142,10 @@ def test_quantisers_match_golden(cuda_dev):
 
 @pytest.mark.parametrize("transpose", [False, True])
 @pytest.mark.parametrize("mode", [bwgemm.SCALE_NONE, bwgemm.SCALE_FIXED8, bwgemm.SCALE_AMAX])
-def test_quantize_fp8_bit_exact(cuda_dev, transpose, mode):
-    x = o.seeded_normal((200, 328), 5) * 3
+@pytest.mark.parametrize("shape", [(200, 328), (256, 96), (4096, 160), (37, 45)])
+def test_quantize_fp8_bit_exact(cuda_dev, transpose, mode, shape):
+    """16-wide vector paths (rows % 16 == 0, n % 16 == 0) and the element-wise fallbacks."""
+    x = o.seeded_normal(shape, 5) * 3
     q, s = bwgemm.quantize_fp8(_t(x, cuda_dev), transpose, mode)
     qr, sr = o.quant_fp8(x, transpose, mode)
     assert np.array_equal(_np(q), qr)
@@ -153,8 +155,9 @@ def test_quantize_fp8_bit_exact(cuda_dev, transpose, mode):
 @pytest.mark.parametrize("transpose", [False, True])
 @pytest.mark.parametrize("container", [bwgemm.FP4_PACKED, bwgemm.FP4_BYTE_SHL2])
 @pytest.mark.parametrize("mode", [bwgemm.SCALE_FIXED8, bwgemm.SCALE_AMAX])
-def test_quantize_fp4_bit_exact(cuda_dev, transpose, container, mode):
-    x = o.seeded_normal((192, 256), 6)
+@pytest.mark.parametrize("shape", [(192, 256), (130, 66)])
+def test_quantize_fp4_bit_exact(cuda_dev, transpose, container, mode, shape):
+    x = o.seeded_normal(shape, 6)
     q, s = bwgemm.quantize_fp4(_t(x, cuda_dev), transpose, mode, container)
     qr, sr = o.quant_fp4(x, transpose, mode, container)
     assert np.array_equal(_np(q), qr)
@@ -163,9 +166,18 @@ def test_quantize_fp4_bit_exact(cuda_dev, transpose, container, mode):
 
 @pytest.mark.parametrize("transpose", [False, True])
 @pytest.mark.parametrize("mode", [bwgemm.MX_UNIT_FIXED8, bwgemm.MX_BLOCK32])
-def test_quantize_mxfp4_bit_exact(cuda_dev, transpose, mode):
-    x = o.seeded_normal((256, 320), 7)
+@pytest.mark.parametrize("shape", [(256, 320), (288, 96), (64, 1312), (4096, 512)])
+def test_quantize_mxfp4_bit_exact(cuda_dev, transpose, mode, shape):
+    """Ragged tails in both directions (K not a multiple of 128 or 256, outer not a multiple
+    of 32 or 128), zero blocks, huge and non-finite values."""
+    x = o.seeded_normal(shape, 7)
     x[:, :7] *= 1e3
+    x[:32, :32] = 0.0
+    x[40, 40] = np.float32(3e38)
+    x[41, 41] = np.inf
+    x[42, 42] = -np.inf
+    x[43, 43] = np.nan
+    x[44, 44] = np.float32(1e-42)
     q, sf = bwgemm.quantize_mxfp4(_t(x, cuda_dev), transpose, mode)
     qr, sfr = o.quant_mxfp4(x, transpose, mode)
     assert np.array_equal(_np(q), qr)

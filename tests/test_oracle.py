@@ -96,6 +96,27 @@ def _build_pin(tmp_path):
     return exe
 
 
+def _build_e2m1_check(tmp_path):
+    here = os.path.join(os.path.dirname(os.path.dirname(__file__)), "oracle")
+    exe = str(tmp_path / "e2m1")
+    subprocess.run(["gcc", "-O2", "-std=c11", "-ffp-contract=off", os.path.join(here, "check_e2m1_fast.c"),
+                    os.path.join(here, "bw_oracle.c"), "-o", exe, "-lm", "-lpthread"], check=True)
+    return exe
+
+
+def test_fast_e2m1_encoder_matches_rule(tmp_path):
+    """The quantisers' table-driven E2M1 encoder equals the reference rule (strided sweep of
+    all bit patterns, every NaN/Inf/subnormal class included; the full sweep is `slow`)."""
+    r = subprocess.run([_build_e2m1_check(tmp_path), "97"], capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout + r.stderr
+
+
+@pytest.mark.slow
+def test_fast_e2m1_encoder_matches_rule_exhaustive(tmp_path):
+    r = subprocess.run([_build_e2m1_check(tmp_path), "1"], capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout + r.stderr
+
+
 def test_mx_scale_rule():
     # block amax in [2^(e+2), 2^(e+3)) -> byte e + 127; all-zero block -> byte 0
     x = np.zeros((1, 128), np.float32)
