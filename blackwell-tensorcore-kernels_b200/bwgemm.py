@@ -91,6 +91,12 @@ def lib():
         "bw_unshard_columns": [P, P, I, I, I, P],
         "bw_unshard_columns_bf16": [P, P, I, I, I, P],
         "bw_gemm_sharded": [I, I, P, I, I, I, I, I],
+        "bw_gemm_f16_allgather": [P, P, P, P, I, I, I, I, I, P],
+        "bw_gemm_fp8_allgather": [P, P, P, P, P, I, P, I, I, I, I, I, P],
+        "bw_ipc_malloc": [ctypes.c_size_t, P, P],
+        "bw_ipc_free": [P],
+        "bw_ipc_open": [P, P],
+        "bw_ipc_close": [P],
     }
     for name, args in sig.items():
         f = getattr(L, name)
@@ -310,3 +316,69 @@ def gemm_sharded(dtype: int, parts: list[dict], M: int, N: int, K: int, out_dtyp
                        _ptr(part.get("C_gathered")), _stream(st))
     _check(lib().bw_gemm_sharded(dtype, out_dtype, ctypes.cast(arr, ctypes.c_void_p) if parts else None,
                                  len(parts), M, N, K, int(gather)))
+
+
+# ------------------------------------------------------------------ fused all-gather (IPC)
+IPC_HANDLE_BYTES = 64
+
+
+class IpcBuffer:
+    """A device buffer other processes can map (CUDA IPC). `tensor` views it as a torch tensor
+    (through __cuda_array_interface__, no copy); `handle` is the 64-byte IPC handle."""
+
+    def __init__(self, shape, dtype, device):
+        import math
+
+        import torch
+
+        self.shape, self.dtype = tuple(shape), dtype
+        nbytes = math.prod(self.shape) * torch.empty((), dtype=dtype).element_size()
+        ptr = ctypes.c_void_p()
+        h = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+        with torch.cuda.device(device):
+            _check(lib().bw_ipc_malloc(nbytes, ctypes.byref(ptr), h))
+        self.ptr, self.handle, self.device = ptr.value, h.raw, torch.device(device)
+        typestr = {torch.float32: "<f4", torch.bfloat16: "<i2", torch.float16: "<f2"}[dtype]
+        self.__cuda_array_interface__ = {"shape": self.shape, "typestr": typestr, "data": (self.ptr, False),
+                                         "version": 3, "strides": None}
+        t = torch.as_tensor(self, device=self.device)
+        self.tensor = t.view(dtype) if dtype == torch.bfloat16 else t
+
+    def close(self):
+        if self.ptr:
+            _check(lib().bw_ipc_free(self.ptr))
+            self.ptr = None
+
+
+def ipc_open(handle: bytes, device) -> int:
+    import torch
+
+    ptr = ctypes.c_void_p()
+    with torch.cuda.device(device):
+        _check(lib().bw_ipc_open(ctypes.create_string_buffer(handle, IPC_HANDLE_BYTES), ctypes.byref(ptr)))
+    return ptr.value
+
+
+def ipc_close(ptr: int) -> None:
+    _check(lib().bw_ipc_close(ptr))
+
+
+def _peer_array(peers):
+    return (ctypes.c_void_p * len(peers))(*[p or 0 for p in peers])
+
+
+def gemm_f16_allgather(A, B_shard, C_full, peers, rank: int, stream=None):
+    """This rank's columns of C_full = A x B_shard, stored locally and into every peer's C_full
+    (peers[q] = rank q's buffer mapped here; entry [rank] ignored)."""
+    M, K = A.shape
+    world = len(peers)
+    _check(lib().bw_gemm_f16_allgather(_ptr(A), _ptr(B_shard), _ptr(C_full), _peer_array(peers), world, rank, M,
+                                       C_full.shape[1], K, _stream(stream)))
+
+
+def gemm_fp8_allgather(A, Bt_shard, scale_a, scale_b, C_full, peers, rank: int, out_dtype=OUT_BF16, stream=None):
+    M, K = A.shape
+    world = len(peers)
+    _check(lib().bw_gemm_fp8_allgather(_ptr(A), _ptr(Bt_shard), _ptr(scale_a), _ptr(scale_b), _ptr(C_full),
+                                       out_dtype, _peer_array(peers), world, rank, M, C_full.shape[1], K,
+                                       _stream(stream)))

@@ -150,6 +150,15 @@ int make_c_map(CUtensorMap* tc, void* C, int M, int N, int out_dtype) {
   return make_tmap_2d(tc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, C, N, M, uint64_t(N) * 4, 32, 32);
 }
 
+// Fused all-gather of column shards: this rank's C columns start at col0 of a row-major
+// M x ldc buffer, and the same bytes go to the same place in each peer's buffer.
+struct GatherCtx {
+  int ldc;
+  int col0;
+  int npeers;
+  void* peers[7];
+};
+
 GemmParams base_params(const DeviceState& d, void* C, int M, int N, int K) {
   GemmParams p{};
   p.C = C;
@@ -257,16 +266,42 @@ int set_splits(GemmParams& p, int splits, int nk) {
   return BW_OK;
 }
 
-int gemm_f16_impl(const void* A, const void* B, float* C, int M, int N, int K, cudaStream_t s, bool b_mn) {
+// With a GatherCtx, C is the row-major M x g->ldc buffer that receives this rank's N columns at
+// g->col0 (and the same bytes go to every peer): the CTA-pair kernel with the direct epilogue.
+int gather_check(const GatherCtx* g, const void* C, int N, int K, int elem) {
+  if (!g) return BW_OK;
+  if (K <= 0) return set_error(BW_ERR_INVALID, "fused gather needs K > 0");
+  if (g->npeers < 0 || g->npeers > 7) return set_error(BW_ERR_INVALID, "fused gather: %d peers (at most 7)", g->npeers);
+  const char* cs = static_cast<const char*>(C) + static_cast<size_t>(g->col0) * elem;
+  if (!direct_epilogue_ok(cs, g->ldc, elem) || (static_cast<long long>(N) * elem) % 32 != 0)
+    return set_error(BW_ERR_INVALID, "fused gather needs 32-byte aligned C, column offset and row pitch "
+                                     "(shard width x element size a multiple of 32)");
+  for (int i = 0; i < g->npeers; ++i)
+    if (!g->peers[i] || (reinterpret_cast<uintptr_t>(g->peers[i]) & 31u))
+      return set_error(BW_ERR_INVALID, "fused gather: peer buffer %d is null or not 32-byte aligned", i);
+  return BW_OK;
+}
+
+void gather_apply(const GatherCtx* g, GemmParams& p, int elem) {
+  if (!g) return;
+  p.C = static_cast<char*>(p.C) + static_cast<size_t>(g->col0) * elem;
+  p.ldc = g->ldc;
+  p.npeers = g->npeers;
+  for (int i = 0; i < g->npeers; ++i) p.peers[i] = static_cast<char*>(g->peers[i]) + static_cast<size_t>(g->col0) * elem;
+}
+
+int gemm_f16_impl(const void* A, const void* B, float* C, int M, int N, int K, cudaStream_t s, bool b_mn,
+                  const GatherCtx* g = nullptr) {
   int r = check_common(A, B, C, M, N, K);
   if (r != BW_OK || M == 0 || N == 0) return r;
   if (K % 8 != 0 || N % 8 != 0)
     return set_error(BW_ERR_INVALID, "fp16 GEMM needs K %% 8 == 0 and N %% 8 == 0 (got N=%d K=%d)", N, K);
+  if ((r = gather_check(g, C, N, K, 4)) != BW_OK) return r;
   DeviceState* d;
   if ((r = ensure_device(&d)) != BW_OK) return r;
   if (K == 0) { BW_CUDA(cudaMemsetAsync(C, 0, sizeof(float) * size_t(M) * N, s)); return BW_OK; }
-  const int splits = choose_splits(M, N, (K + 63) / 64, 4, *d);
-  const bool pair = splits == 1 && use_pair(M, N, *d);
+  const int splits = g ? 1 : choose_splits(M, N, (K + 63) / 64, 4, *d);
+  const bool pair = g || (splits == 1 && use_pair(M, N, *d));
   const bool narrow = !pair && splits == 1 && use_narrow(M, N, *d);
   const int bn = pair ? 128 : narrow ? 128 : 256;
   CUtensorMap ta, tb;
@@ -277,8 +312,9 @@ int gemm_f16_impl(const void* A, const void* B, float* C, int M, int N, int K, c
   CUtensorMap tc;
   if ((r = make_c_map(&tc, C, M, N, BW_OUT_F32)) != BW_OK) return r;
   GemmParams p = base_params(*d, C, M, N, K);
+  gather_apply(g, p, 4);
   if (pair) {
-    if (direct_epilogue_ok(C, N, 4)) {
+    if (g || direct_epilogue_ok(C, N, 4)) {
       if (b_mn) return launch_pair<Kind::F16, true, 3, Out::F32, true, 2>(ta, tb, tc, p, s, *d);
       return launch_pair<Kind::F16, false, 3, Out::F32, true, 2>(ta, tb, tc, p, s, *d);
     }
@@ -299,17 +335,18 @@ int gemm_f16_impl(const void* A, const void* B, float* C, int M, int N, int K, c
 }
 
 int gemm_fp8_impl(const uint8_t* A, const uint8_t* Bt, const float* sa, const float* sb, void* C, int out_dtype,
-                  int M, int N, int K, cudaStream_t s) {
+                  int M, int N, int K, cudaStream_t s, const GatherCtx* g = nullptr) {
   int r = check_common(A, Bt, C, M, N, K);
   if (r != BW_OK || M == 0 || N == 0) return r;
   if (out_dtype != BW_OUT_F32 && out_dtype != BW_OUT_BF16) return set_error(BW_ERR_INVALID, "bad out_dtype %d", out_dtype);
   if (K % 16 != 0) return set_error(BW_ERR_INVALID, "fp8 GEMM needs K %% 16 == 0 (got %d)", K);
   if (N % 8 != 0) return set_error(BW_ERR_INVALID, "fp8 GEMM needs N %% 8 == 0 (got %d)", N);
+  if ((r = gather_check(g, C, N, K, static_cast<int>(out_elem_bytes(out_dtype)))) != BW_OK) return r;
   DeviceState* d;
   if ((r = ensure_device(&d)) != BW_OK) return r;
   if (K == 0) { BW_CUDA(cudaMemsetAsync(C, 0, out_elem_bytes(out_dtype) * size_t(M) * N, s)); return BW_OK; }
-  const int splits = choose_splits(M, N, (K + 127) / 128, static_cast<int>(out_elem_bytes(out_dtype)), *d);
-  const bool pair = splits == 1 && use_pair(M, N, *d);
+  const int splits = g ? 1 : choose_splits(M, N, (K + 127) / 128, static_cast<int>(out_elem_bytes(out_dtype)), *d);
+  const bool pair = g || (splits == 1 && use_pair(M, N, *d));
   const bool narrow = !pair && splits == 1 && use_narrow(M, N, *d);
   const int bn = pair ? 128 : narrow ? 128 : 256;
   CUtensorMap ta, tb;
@@ -318,10 +355,11 @@ int gemm_fp8_impl(const uint8_t* A, const uint8_t* Bt, const float* sa, const fl
   CUtensorMap tc;
   if ((r = make_c_map(&tc, C, M, N, out_dtype)) != BW_OK) return r;
   GemmParams p = base_params(*d, C, M, N, K);
+  gather_apply(g, p, static_cast<int>(out_elem_bytes(out_dtype)));
   p.scale_a = sa;
   p.scale_b = sb;
   if (pair) {
-    const bool direct = direct_epilogue_ok(C, N, static_cast<int>(out_elem_bytes(out_dtype)));
+    const bool direct = g || direct_epilogue_ok(C, N, static_cast<int>(out_elem_bytes(out_dtype)));
     if (out_dtype == BW_OUT_F32) {
       if (direct) return launch_pair<Kind::F8, false, 3, Out::F32, true, 2>(ta, tb, tc, p, s, *d);
       return launch_pair<Kind::F8, false, 3, Out::F32, false, 2>(ta, tb, tc, p, s, *d);
@@ -423,6 +461,37 @@ int bw_gemm_f16(const void* A, const void* B, float* C, int M, int N, int K, voi
 
 int bw_gemm_f16_bt(const void* A, const void* Bt, float* C, int M, int N, int K, void* stream) {
   return gemm_f16_impl(A, Bt, C, M, N, K, static_cast<cudaStream_t>(stream), false);
+}
+
+static int make_gather(GatherCtx* g, void* const* peer_C_full, int world, int rank, int N_total) {
+  if (world < 1 || world > 8 || rank < 0 || rank >= world)
+    return set_error(BW_ERR_INVALID, "fused gather: rank %d of world %d (1..8 ranks)", rank, world);
+  if (N_total % world != 0) return set_error(BW_ERR_INVALID, "N_total=%d not divisible by world=%d", N_total, world);
+  if (world > 1 && !peer_C_full) return set_error(BW_ERR_INVALID, "fused gather: peer_C_full is null");
+  g->ldc = N_total;
+  g->col0 = rank * (N_total / world);
+  g->npeers = 0;
+  for (int q = 0; q < world; ++q)
+    if (q != rank) g->peers[g->npeers++] = peer_C_full[q];
+  return BW_OK;
+}
+
+int bw_gemm_f16_allgather(const void* A, const void* B_shard, float* C_full, void* const* peer_C_full, int world,
+                          int rank, int M, int N_total, int K, void* stream) {
+  GatherCtx g;
+  int r = make_gather(&g, peer_C_full, world, rank, N_total);
+  if (r != BW_OK) return r;
+  return gemm_f16_impl(A, B_shard, C_full, M, N_total / world, K, static_cast<cudaStream_t>(stream), true, &g);
+}
+
+int bw_gemm_fp8_allgather(const uint8_t* A, const uint8_t* Bt_shard, const float* scale_a, const float* scale_b,
+                          void* C_full, int out_dtype, void* const* peer_C_full, int world, int rank, int M,
+                          int N_total, int K, void* stream) {
+  GatherCtx g;
+  int r = make_gather(&g, peer_C_full, world, rank, N_total);
+  if (r != BW_OK) return r;
+  return gemm_fp8_impl(A, Bt_shard, scale_a, scale_b, C_full, out_dtype, M, N_total / world, K,
+                       static_cast<cudaStream_t>(stream), &g);
 }
 
 int bw_gemm_fp8(const uint8_t* A, const uint8_t* Bt, const float* scale_a, const float* scale_b, void* C,

@@ -81,6 +81,10 @@ struct GemmParams {
   int* status;                 // device status word
   unsigned long long* trace;   // optional per-CTA wait-time trace (kTraceWords per CTA), or null
   unsigned long long budget_ns;
+  // Fused all-gather (direct epilogue only): every stored 32-byte piece of C also goes to the
+  // same offset from each peers[i] (another GPU's copy of C, opened through CUDA IPC).
+  void* peers[7];
+  int npeers;
 };
 
 template <Kind KIND, bool B_MN, int BN, int STAGES, int ACC_BUFS>
@@ -151,6 +155,8 @@ __device__ __forceinline__ void epilogue_tile_direct(uint32_t tbase, const GemmP
         for (int j = 0; j < 8; ++j) v[j] = __float_as_uint(__uint_as_float(r[8 * g + j]) * alpha);
         if (stream_out) st_global_v8_hint(dst + 8 * g, v, pol);
         else st_global_v8(dst + 8 * g, v);
+        for (int i = 0; i < p.npeers; ++i)
+          st_global_v8(static_cast<float*>(p.peers[i]) + (dst + 8 * g - static_cast<float*>(p.C)), v);
       }
     } else {
       __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.C) + static_cast<size_t>(row) * p.ldc + col;
@@ -167,8 +173,13 @@ __device__ __forceinline__ void epilogue_tile_direct(uint32_t tbase, const GemmP
         if (col + 16 * g + 16 <= p.N) {
           if (stream_out) st_global_v8_hint(dst + 16 * g, v, pol);
           else st_global_v8(dst + 16 * g, v);
+          for (int i = 0; i < p.npeers; ++i)
+            st_global_v8(static_cast<__nv_bfloat16*>(p.peers[i]) + (dst + 16 * g - static_cast<__nv_bfloat16*>(p.C)), v);
         } else {  // N % 16 == 8: the last group holds 8 valid columns
           *reinterpret_cast<uint4*>(dst + 16 * g) = make_uint4(v[0], v[1], v[2], v[3]);
+          for (int i = 0; i < p.npeers; ++i)
+            *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.peers[i]) +
+                                      (dst + 16 * g - static_cast<__nv_bfloat16*>(p.C))) = make_uint4(v[0], v[1], v[2], v[3]);
         }
       }
     }

@@ -6,6 +6,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "bw_ptx.cuh"
@@ -188,6 +189,47 @@ int bw_shutdown(void) {
     d = DeviceState{};
   }
   cudaSetDevice(cur);
+  return BW_OK;
+}
+
+int bw_ipc_malloc(size_t bytes, void** ptr, void* handle_out) {
+  if (!ptr || !handle_out || bytes == 0) return set_error(BW_ERR_INVALID, "bw_ipc_malloc: bad arguments");
+  DeviceState* d;
+  int r = ensure_device(&d);
+  if (r != BW_OK) return r;
+  BW_CUDA(cudaMalloc(ptr, bytes));
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, *ptr);
+  if (e != cudaSuccess) {
+    cudaFree(*ptr);
+    *ptr = nullptr;
+    return cuda_error(e, "cudaIpcGetMemHandle");
+  }
+  static_assert(sizeof(h) == BW_IPC_HANDLE_BYTES, "IPC handle size");
+  memcpy(handle_out, &h, sizeof(h));
+  return BW_OK;
+}
+
+int bw_ipc_free(void* ptr) {
+  if (!ptr) return BW_OK;
+  BW_CUDA(cudaFree(ptr));
+  return BW_OK;
+}
+
+int bw_ipc_open(const void* handle, void** peer_ptr) {
+  if (!handle || !peer_ptr) return set_error(BW_ERR_INVALID, "bw_ipc_open: bad arguments");
+  DeviceState* d;
+  int r = ensure_device(&d);
+  if (r != BW_OK) return r;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  BW_CUDA(cudaIpcOpenMemHandle(peer_ptr, h, cudaIpcMemLazyEnablePeerAccess));
+  return BW_OK;
+}
+
+int bw_ipc_close(void* peer_ptr) {
+  if (!peer_ptr) return BW_OK;
+  BW_CUDA(cudaIpcCloseMemHandle(peer_ptr));
   return BW_OK;
 }
 

@@ -49,3 +49,31 @@ def gather_columns(C_local, world: int, group=None):
     buf = torch.empty((world * M, ns), dtype=C_local.dtype, device=C_local.device)
     dist.all_gather_into_tensor(buf, C_local.contiguous(), group=group)
     return unshard(buf, M, ns * world, world)
+
+
+class SymmetricC:
+    """Row-major M x N_total C that every rank holds in an IPC-shareable buffer, plus the peers'
+    buffers mapped into this process: the target of the fused GEMM + all-gather
+    (bwgemm.gemm_*_allgather). Handles are exchanged with torch.distributed.all_gather_object."""
+
+    def __init__(self, M: int, N_total: int, dtype, device, world: int, rank: int, group=None):
+        import torch.distributed as dist
+
+        import bwgemm
+
+        self.buf = bwgemm.IpcBuffer((M, N_total), dtype, device)
+        self.C = self.buf.tensor
+        self.rank, self.world = rank, world
+        handles = [None] * world
+        if world > 1:
+            dist.all_gather_object(handles, self.buf.handle, group=group)
+        self.peers = [None if q == rank else bwgemm.ipc_open(handles[q], device) for q in range(world)]
+
+    def close(self):
+        import bwgemm
+
+        for p in self.peers:
+            if p:
+                bwgemm.ipc_close(p)
+        self.peers = []
+        self.buf.close()

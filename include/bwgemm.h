@@ -157,6 +157,29 @@ int bw_unshard_columns(const float* C_shardmajor, float* C_rowmajor, int M, int 
 /* The same permutation for 2-byte elements (BF16 C). */
 int bw_unshard_columns_bf16(const void* C_shardmajor, void* C_rowmajor, int M, int N, int world, void* stream);
 
+/* Fused all-gather (one process per GPU). Every rank holds a row-major M x N_total C_full and the
+ * peers' C_full opened through CUDA IPC (bw_ipc_*); rank r computes columns
+ * [r*N_total/world, (r+1)*N_total/world) from its B shard and its epilogue stores each 32-byte
+ * piece into its own C_full and into every peer's, so when all ranks' calls have completed (the
+ * caller synchronises, then barriers across ranks) every C_full holds the whole product: no
+ * separate collective and no unshard pass. peer_C_full[q] is rank q's buffer as mapped here
+ * (entry [rank] is ignored). Needs 32-byte aligned buffers and a shard width whose rows are
+ * whole 32-byte pieces (N_total/world % 8 == 0 for FP32 C, % 16 for BF16). The single-GPU math
+ * is bw_gemm_f16 / bw_gemm_fp8 (B_shard: K x N_total/world FP16; Bt_shard: N_total/world x K). */
+int bw_gemm_f16_allgather(const void* A, const void* B_shard, float* C_full, void* const* peer_C_full, int world,
+                          int rank, int M, int N_total, int K, void* stream);
+int bw_gemm_fp8_allgather(const uint8_t* A, const uint8_t* Bt_shard, const float* scale_a, const float* scale_b,
+                          void* C_full, int out_dtype, void* const* peer_C_full, int world, int rank, int M,
+                          int N_total, int K, void* stream);
+
+/* Device buffers shareable across processes (CUDA IPC, 64-byte handles): bw_ipc_malloc returns
+ * the buffer (256-byte aligned) and its handle; another process maps it with bw_ipc_open. */
+enum { BW_IPC_HANDLE_BYTES = 64 };
+int bw_ipc_malloc(size_t bytes, void** ptr, void* handle_out);
+int bw_ipc_free(void* ptr);
+int bw_ipc_open(const void* handle, void** peer_ptr);
+int bw_ipc_close(void* peer_ptr);
+
 /* One process driving g GPUs of a node (the single-process form of the sharded run).
  * Shard r lives on `device` and holds the full A plus columns [r*N/g, (r+1)*N/g) of B in the
  * layout the dtype's single-GPU entry point takes:
