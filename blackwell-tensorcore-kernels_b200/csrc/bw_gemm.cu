@@ -40,7 +40,8 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, 
 
 template <Kind KIND, bool B_MN, int STAGES, Out OUT, bool DIRECT_EPI, int KSUB, int TN = 256>
 int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, GemmParams p,
-                cudaStream_t stream, const DeviceState& d) {
+                cudaStream_t stream, const DeviceState& d, const PeerMaps* pm = nullptr) {
+  static const PeerMaps no_peers{};
   using Cfg = PairCfg<KIND, STAGES, DIRECT_EPI, KSUB, TN>;
   auto kern = bw_tc_gemm_pair_kernel<KIND, B_MN, STAGES, OUT, DIRECT_EPI, KSUB, TN>;
   static bool attr_done[64] = {};
@@ -78,7 +79,7 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
   const int cap = env_int("BW_MAX_CTAS", 0);
   if (cap > 1 && clusters > cap / 2) clusters = cap / 2;
   p.trace = trace_buffer(2 * clusters);
-  kern<<<2 * clusters, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, tc, p);
+  kern<<<2 * clusters, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, tc, pm ? *pm : no_peers, p);
   BW_CUDA(cudaGetLastError());
   return BW_OK;
 }
@@ -144,6 +145,13 @@ int launch_pair_mx(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorM
 }
 
 // Output tensor map for the TMA-store epilogue: 32 rows x 128 B boxes, 128B swizzle.
+// C map with an explicit row pitch (elements), e.g. one column shard inside a wider C.
+int make_c_map_ld(CUtensorMap* tc, void* C, int M, int N, int ld, int out_dtype) {
+  if (out_dtype == BW_OUT_BF16)
+    return make_tmap_2d(tc, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, C, N, M, uint64_t(ld) * 2, 64, 32);
+  return make_tmap_2d(tc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, C, N, M, uint64_t(ld) * 4, 32, 32);
+}
+
 int make_c_map(CUtensorMap* tc, void* C, int M, int N, int out_dtype) {
   if (out_dtype == BW_OUT_BF16)
     return make_tmap_2d(tc, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, C, N, M, uint64_t(N) * 2, 64, 32);
@@ -267,18 +275,19 @@ int set_splits(GemmParams& p, int splits, int nk) {
 }
 
 // With a GatherCtx, C is the row-major M x g->ldc buffer that receives this rank's N columns at
-// g->col0 (and the same bytes go to every peer): the CTA-pair kernel with the direct epilogue.
+// g->col0, and every peer receives the same: the CTA-pair kernel with the staged (TMA-store)
+// epilogue and one extra tensor map per peer. TMA needs 16-byte aligned bases and row pitches.
 int gather_check(const GatherCtx* g, const void* C, int N, int K, int elem) {
   if (!g) return BW_OK;
   if (K <= 0) return set_error(BW_ERR_INVALID, "fused gather needs K > 0");
   if (g->npeers < 0 || g->npeers > 7) return set_error(BW_ERR_INVALID, "fused gather: %d peers (at most 7)", g->npeers);
-  const char* cs = static_cast<const char*>(C) + static_cast<size_t>(g->col0) * elem;
-  if (!direct_epilogue_ok(cs, g->ldc, elem) || (static_cast<long long>(N) * elem) % 32 != 0)
-    return set_error(BW_ERR_INVALID, "fused gather needs 32-byte aligned C, column offset and row pitch "
-                                     "(shard width x element size a multiple of 32)");
+  const size_t off = static_cast<size_t>(g->col0) * elem;
+  if (((reinterpret_cast<uintptr_t>(C) + off) & 15u) || (static_cast<size_t>(g->ldc) * elem) % 16 != 0 ||
+      (static_cast<size_t>(N) * elem) % 16 != 0)
+    return set_error(BW_ERR_INVALID, "fused gather needs 16-byte aligned C, column offset and row pitch");
   for (int i = 0; i < g->npeers; ++i)
-    if (!g->peers[i] || (reinterpret_cast<uintptr_t>(g->peers[i]) & 31u))
-      return set_error(BW_ERR_INVALID, "fused gather: peer buffer %d is null or not 32-byte aligned", i);
+    if (!g->peers[i] || (reinterpret_cast<uintptr_t>(g->peers[i]) & 15u))
+      return set_error(BW_ERR_INVALID, "fused gather: peer buffer %d is null or not 16-byte aligned", i);
   return BW_OK;
 }
 
@@ -313,8 +322,16 @@ int gemm_f16_impl(const void* A, const void* B, float* C, int M, int N, int K, c
   if ((r = make_c_map(&tc, C, M, N, BW_OUT_F32)) != BW_OK) return r;
   GemmParams p = base_params(*d, C, M, N, K);
   gather_apply(g, p, 4);
+  if (g) {
+    PeerMaps pm{};
+    CUtensorMap tcl;
+    if ((r = make_c_map_ld(&tcl, p.C, M, N, g->ldc, BW_OUT_F32)) != BW_OK) return r;
+    for (int q = 0; q < p.npeers; ++q)
+      if ((r = make_c_map_ld(&pm.m[q], p.peers[q], M, N, g->ldc, BW_OUT_F32)) != BW_OK) return r;
+    return launch_pair<Kind::F16, true, 3, Out::F32, false, 2>(ta, tb, tcl, p, s, *d, &pm);
+  }
   if (pair) {
-    if (g || direct_epilogue_ok(C, N, 4)) {
+    if (direct_epilogue_ok(C, N, 4)) {
       if (b_mn) return launch_pair<Kind::F16, true, 3, Out::F32, true, 2>(ta, tb, tc, p, s, *d);
       return launch_pair<Kind::F16, false, 3, Out::F32, true, 2>(ta, tb, tc, p, s, *d);
     }
@@ -358,8 +375,17 @@ int gemm_fp8_impl(const uint8_t* A, const uint8_t* Bt, const float* sa, const fl
   gather_apply(g, p, static_cast<int>(out_elem_bytes(out_dtype)));
   p.scale_a = sa;
   p.scale_b = sb;
+  if (g) {
+    PeerMaps pm{};
+    CUtensorMap tcl;
+    if ((r = make_c_map_ld(&tcl, p.C, M, N, g->ldc, out_dtype)) != BW_OK) return r;
+    for (int q = 0; q < p.npeers; ++q)
+      if ((r = make_c_map_ld(&pm.m[q], p.peers[q], M, N, g->ldc, out_dtype)) != BW_OK) return r;
+    if (out_dtype == BW_OUT_F32) return launch_pair<Kind::F8, false, 3, Out::F32, false, 2>(ta, tb, tcl, p, s, *d, &pm);
+    return launch_pair<Kind::F8, false, 3, Out::BF16, false, 2>(ta, tb, tcl, p, s, *d, &pm);
+  }
   if (pair) {
-    const bool direct = g || direct_epilogue_ok(C, N, static_cast<int>(out_elem_bytes(out_dtype)));
+    const bool direct = direct_epilogue_ok(C, N, static_cast<int>(out_elem_bytes(out_dtype)));
     if (out_dtype == BW_OUT_F32) {
       if (direct) return launch_pair<Kind::F8, false, 3, Out::F32, true, 2>(ta, tb, tc, p, s, *d);
       return launch_pair<Kind::F8, false, 3, Out::F32, false, 2>(ta, tb, tc, p, s, *d);

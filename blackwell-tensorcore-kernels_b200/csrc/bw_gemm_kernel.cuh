@@ -81,8 +81,8 @@ struct GemmParams {
   int* status;                 // device status word
   unsigned long long* trace;   // optional per-CTA wait-time trace (kTraceWords per CTA), or null
   unsigned long long budget_ns;
-  // Fused all-gather (direct epilogue only): every stored 32-byte piece of C also goes to the
-  // same offset from each peers[i] (another GPU's copy of C, opened through CUDA IPC).
+  // Fused all-gather (staged epilogue): peers[i] is another GPU's copy of C (opened through
+  // CUDA IPC) at this shard's column offset; each staged chunk is also TMA-stored there.
   void* peers[7];
   int npeers;
 };
@@ -155,8 +155,6 @@ __device__ __forceinline__ void epilogue_tile_direct(uint32_t tbase, const GemmP
         for (int j = 0; j < 8; ++j) v[j] = __float_as_uint(__uint_as_float(r[8 * g + j]) * alpha);
         if (stream_out) st_global_v8_hint(dst + 8 * g, v, pol);
         else st_global_v8(dst + 8 * g, v);
-        for (int i = 0; i < p.npeers; ++i)
-          st_global_v8(static_cast<float*>(p.peers[i]) + (dst + 8 * g - static_cast<float*>(p.C)), v);
       }
     } else {
       __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.C) + static_cast<size_t>(row) * p.ldc + col;
@@ -173,23 +171,26 @@ __device__ __forceinline__ void epilogue_tile_direct(uint32_t tbase, const GemmP
         if (col + 16 * g + 16 <= p.N) {
           if (stream_out) st_global_v8_hint(dst + 16 * g, v, pol);
           else st_global_v8(dst + 16 * g, v);
-          for (int i = 0; i < p.npeers; ++i)
-            st_global_v8(static_cast<__nv_bfloat16*>(p.peers[i]) + (dst + 16 * g - static_cast<__nv_bfloat16*>(p.C)), v);
         } else {  // N % 16 == 8: the last group holds 8 valid columns
           *reinterpret_cast<uint4*>(dst + 16 * g) = make_uint4(v[0], v[1], v[2], v[3]);
-          for (int i = 0; i < p.npeers; ++i)
-            *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.peers[i]) +
-                                      (dst + 16 * g - static_cast<__nv_bfloat16*>(p.C))) = make_uint4(v[0], v[1], v[2], v[3]);
         }
       }
     }
   }
 }
 
+// Tensor maps over the peers' copies of C for the fused all-gather (staged epilogue): each
+// staged 32-row chunk leaves through one TMA store per destination, so the copy engine, not the
+// epilogue warps, carries the NVLink traffic.
+struct PeerMaps {
+  CUtensorMap m[7];
+};
+
 template <Out OUT, int NCOLS, typename Release>
 __device__ __forceinline__ void epilogue_tile(uint32_t tbase, const CUtensorMap* tmC, int x0, int y0, float alpha,
                                               uint8_t* wbuf, int& uses, int lane, uint64_t store_policy,
-                                              bool hinted, Release release, bool reduce_add = false) {
+                                              bool hinted, Release release, bool reduce_add = false,
+                                              const PeerMaps* peer_maps = nullptr, int npeers = 0) {
   constexpr int kCols = (OUT == Out::F32) ? 32 : 64;  // columns per 128-byte row chunk
   static_assert(NCOLS % kCols == 0, "tile width must be whole 128-byte chunks");
   const uint32_t row_addr = smem_u32(wbuf) + lane * 128;
@@ -231,6 +232,7 @@ __device__ __forceinline__ void epilogue_tile(uint32_t tbase, const CUtensorMap*
       if (reduce_add) tma_reduce_add_2d(tmC, wbuf + bsel * kEpiBufBytes, x0 + c, y0);
       else if (hinted) tma_store_2d_hint(tmC, wbuf + bsel * kEpiBufBytes, x0 + c, y0, store_policy);
       else tma_store_2d(tmC, wbuf + bsel * kEpiBufBytes, x0 + c, y0);
+      for (int q = 0; q < npeers; ++q) tma_store_2d(&peer_maps->m[q], wbuf + bsel * kEpiBufBytes, x0 + c, y0);
       bulk_commit_group();
     }
     ++uses;

@@ -42,7 +42,8 @@ struct PairCfg {
 template <Kind KIND, bool B_MN, int STAGES, Out OUT, bool DIRECT_EPI, int KSUB, int TN = 256>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     bw_tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                           const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
+                           const __grid_constant__ CUtensorMap tmC, const __grid_constant__ PeerMaps pm,
+                           const GemmParams p) {
   using Cfg = PairCfg<KIND, STAGES, DIRECT_EPI, KSUB, TN>;
   static_assert(!B_MN || TN == 256, "N-major B is loaded as 64-column boxes of a 256-wide tile");
   constexpr int KX = KindTraits<KIND>::kCoordPerSlab;          // tensor-map units per swizzle atom
@@ -218,7 +219,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const int row0 = tm * TM + static_cast<int>(rank) * 128 + q * 32;
       if constexpr (DIRECT_EPI) epilogue_tile_direct<OUT, TN>(tbase, p, row0 + lane, tn * TN, alpha, release);
       else epilogue_tile<OUT, TN>(tbase, &tmC, tn * TN, row0, alpha, wbuf, uses, lane, store_pol,
-                                  (p.hints & 2) != 0, release);
+                                  (p.hints & 2) != 0, release, false, &pm, p.npeers);
       if (tracing) { tr_b += clock64() - w4; ++tr_c; }
     }
     if (lane == 0) bulk_wait_group<0>();

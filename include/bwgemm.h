@@ -159,13 +159,13 @@ int bw_unshard_columns_bf16(const void* C_shardmajor, void* C_rowmajor, int M, i
 
 /* Fused all-gather (one process per GPU). Every rank holds a row-major M x N_total C_full and the
  * peers' C_full opened through CUDA IPC (bw_ipc_*); rank r computes columns
- * [r*N_total/world, (r+1)*N_total/world) from its B shard and its epilogue stores each 32-byte
- * piece into its own C_full and into every peer's, so when all ranks' calls have completed (the
+ * [r*N_total/world, (r+1)*N_total/world) from its B shard, and its epilogue sends every staged
+ * 32-row chunk of the result out through TMA stores to its own C_full and to each peer's, so
+ * the NVLink transfer overlaps the math tile by tile. When all ranks' calls have completed (the
  * caller synchronises, then barriers across ranks) every C_full holds the whole product: no
- * separate collective and no unshard pass. peer_C_full[q] is rank q's buffer as mapped here
- * (entry [rank] is ignored). Needs 32-byte aligned buffers and a shard width whose rows are
- * whole 32-byte pieces (N_total/world % 8 == 0 for FP32 C, % 16 for BF16). The single-GPU math
- * is bw_gemm_f16 / bw_gemm_fp8 (B_shard: K x N_total/world FP16; Bt_shard: N_total/world x K). */
+ * separate collective, no unshard pass. peer_C_full[q] is rank q's buffer as mapped here (entry
+ * [rank] is ignored). Needs 16-byte aligned buffers, column offset and row pitch. The per-rank
+ * math is bw_gemm_f16 / bw_gemm_fp8 (B_shard: K x N_total/world FP16; Bt_shard: N_total/world x K). */
 int bw_gemm_f16_allgather(const void* A, const void* B_shard, float* C_full, void* const* peer_C_full, int world,
                           int rank, int M, int N_total, int K, void* stream);
 int bw_gemm_fp8_allgather(const uint8_t* A, const uint8_t* Bt_shard, const float* scale_a, const float* scale_b,
