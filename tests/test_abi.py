@@ -75,3 +75,18 @@ def test_sharded_argument_validation_without_gpu():
     assert b"sfA" in L.bw_last_error_string()
     nul = [S(0, None, p, None, None, None, None, p, None, None)]
     assert call(0, 0, nul, 8, 8, 8, 0) == bwgemm.BW_ERR_INVALID                     # A null
+
+
+def test_allgather_and_ipc_argument_validation_without_gpu():
+    L = bwgemm.lib()
+    buf = ctypes.create_string_buffer(256)
+    p = (ctypes.addressof(buf) + 31) & ~31
+    peers = (ctypes.c_void_p * 2)(p, p)
+    assert L.bw_gemm_f16_allgather(p, p, p, peers, 0, 0, 8, 16, 8, None) == bwgemm.BW_ERR_INVALID  # world 0
+    assert L.bw_gemm_f16_allgather(p, p, p, peers, 2, 2, 8, 16, 8, None) == bwgemm.BW_ERR_INVALID  # rank >= world
+    assert L.bw_gemm_f16_allgather(p, p, p, peers, 2, 0, 8, 15, 8, None) == bwgemm.BW_ERR_INVALID  # N_total % world
+    assert L.bw_gemm_f16_allgather(p, p, p, None, 2, 0, 8, 16, 8, None) == bwgemm.BW_ERR_INVALID   # no peers
+    assert L.bw_gemm_fp8_allgather(p, p, None, None, p, 1, peers, 9, 0, 8, 16, 16, None) == bwgemm.BW_ERR_INVALID
+    assert L.bw_ipc_malloc(0, None, None) == bwgemm.BW_ERR_INVALID
+    assert L.bw_ipc_open(None, None) == bwgemm.BW_ERR_INVALID
+    assert L.bw_ipc_free(None) == bwgemm.BW_OK and L.bw_ipc_close(None) == bwgemm.BW_OK
