@@ -406,6 +406,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
   if (tracing && lane == 0) {
     unsigned long long* tr = p.trace + static_cast<size_t>(blockIdx.x) * kTraceWords;
     if (warp == 0) tr[3] = tr_a;
+    // words as in the other kernels except 6 (MMA thread: cycles from committing a finished
+    // accumulator to seeing it free again) and 7 (epilogue: TMEM -> register drain cycles)
     if (warp == 1 && leader) { tr[1] = tr_a; tr[2] = tr_b; tr[6] = tr_c; }
     if (warp == 2) { tr[4] = tr_a; tr[5] = tr_b; tr[7] = tr_c; }
   }
