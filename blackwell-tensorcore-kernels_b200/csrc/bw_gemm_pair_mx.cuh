@@ -2,17 +2,19 @@
 //
 // Replaces gemm_lowprec_t<MXFP4> / <FP4> (src/gemm_mma_fp8.cu:89-223, 305-317) for large
 // problems. Structure as bw_tc_gemm_pair_kernel (bw_gemm_pair.cuh) with these differences:
-//   * every stage also carries the scale factors: each CTA loads the SF atoms of its own 128 A
-//     rows and of all 256 B rows of the tile (both CTAs' tensor cores scale the full N); the
-//     leader's MMA thread copies them to Tensor Memory with tcgen05.cp.cta_group::2 (each CTA
-//     from its own shared memory) before the stage's MMAs;
-//   * Tensor Memory holds one 256-column FP32 accumulator plus 48 scale-factor columns (two
+//   * scale factors travel apart from A/B: a loader warp (both CTAs) TMA-loads each stage's SF
+//     atoms - this CTA's 128 A rows and all 256 B rows of the tile, since both CTAs' tensor
+//     cores scale the full N - into a 4-slot shared-memory ring (sf_full / sf_empty), and a
+//     copier warp (leader) moves them with tcgen05.cp.cta_group::2 (each CTA from its own shared
+//     memory) into one of kSfBufs TMEM column buffers (sf_ready / sf_free), so the copies run
+//     ahead of the A/B data and the MMA thread issues only MMAs and commits;
+//   * Tensor Memory holds one 256-column FP32 accumulator plus the scale-factor buffers (two
 //     accumulators would leave no room), so 8 epilogue warps drain the accumulator into
-//     registers (128 columns each), release it at once and convert/store while the next tile
-//     already accumulates.
-// Stage = 2 K atoms (512 FP4 values): A 32 KB + B 32 KB + SFA 2 KB + SFB 4 KB per CTA, 3 stages.
-// With null scale-factor pointers (plain FP4, per-tensor scales only) the 0x7f-filled scale
-// slots are copied once and every block scale stays 2^0.
+//     registers (128 columns each), release it at once (CTA-scope arrive) and convert/store
+//     while the next tile already accumulates.
+// A/B stage = 2 K atoms (512 FP4 values): A 32 KB + B 32 KB per CTA, 3 stages; SF slot = SFA
+// 2 KB + SFB 4 KB. With null scale-factor pointers (plain FP4, per-tensor scales only) the
+// 0x7f-filled slot 0 is copied once and every block scale stays 2^0.
 #pragma once
 #include "bw_gemm_kernel.cuh"
 
