@@ -56,3 +56,46 @@ def test_shard_bounds_and_unshard_cpu():
     full = torch.arange(M * N).reshape(M, N).float()
     shardmajor = torch.stack([full[:, r * 2:(r + 1) * 2] for r in range(world)])
     assert torch.equal(sharding.unshard(shardmajor, M, N, world), full)
+
+
+def _failing_worker(rank, world, port, q):
+    """Rank 1 leaves before the gather (an exception on the host, between steps); rank 0's
+    gather must end with an error within the process group's timeout instead of hanging."""
+    import datetime
+    import time
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=3))
+    if rank == 1:
+        q.put((rank, "left"))
+        q.close()
+        q.join_thread()
+        os._exit(0)  # no destroy_process_group, no gather: the peer simply disappears
+    t0 = time.time()
+    try:
+        sharding.gather_columns(torch.ones(4, 8), world)
+        q.put((rank, "no error"))
+    except Exception as e:  # gloo reports the lost peer (timeout or connection closed)
+        q.put((rank, f"error after {time.time() - t0:.1f}s: {type(e).__name__}"))
+    q.close()
+    q.join_thread()
+    os._exit(0)
+
+
+def test_gather_reports_a_lost_rank_instead_of_hanging():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    results = {}
+    for _ in range(2):
+        r, msg = q.get(timeout=10)
+        results[r] = msg
+    assert results[1] == "left"
+    assert results[0].startswith("error after"), results
