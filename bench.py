@@ -178,7 +178,7 @@ def timed_steps(step, K: int, W: int, world: int, stream):
     return max_over_ranks(ms, world)
 
 
-def fused_gather(args, wl, inp, v, full, world, rank, dev, stream, flops):
+def fused_gather(args, wl, operands, C, full, world, rank, dev, stream, flops):
     """GEMM and all-gather in one kernel: every rank's epilogue stores its columns into its own
     and every peer's IPC-mapped row-major C (bw_gemm_*_allgather). Timed like the GEMM (device
     events, max over ranks, after a barrier); checked bit-for-bit against the NCCL gather."""
@@ -187,14 +187,13 @@ def fused_gather(args, wl, inp, v, full, world, rank, dev, stream, flops):
     import bwgemm
     import sharding
 
-    C = v["C"]
     M, N = C.shape
     sym = sharding.SymmetricC(M, N * world, C.dtype, dev, world, rank)
     if wl == "f16":
-        A, B = inp["A"], inp["B"]
+        A, B = operands
         step = lambda: bwgemm.gemm_f16_allgather(A, B, sym.C, sym.peers, rank, stream=stream)  # noqa: E731
     else:
-        qa, qb, sa, sb = v["qa"], v["qb"], v["sa"], v["sb"]
+        qa, qb, sa, sb = operands
         step = lambda: bwgemm.gemm_fp8_allgather(qa, qb, sa, sb, sym.C, sym.peers, rank, stream=stream)  # noqa: E731
     ms = timed_steps(step, args.steps, args.warmup, world, stream)
     torch.cuda.synchronize()
@@ -394,7 +393,8 @@ def run_ours(args, world, rank, local):
         gather = {"ms": round(gms, 3), "bytes_per_rank": int(C.numel() * C.element_size() * (world - 1)),
                   "layout": "row-major M x N after bw_unshard_columns", "own_shard_intact": ok}
         if wl in ("f16", "fp8"):
-            gather["fused"] = fused_gather(args, wl, inp, locals(), full, world, rank, dev, stream, flops)
+            operands = (inp["A"], inp["B"]) if wl == "f16" else (qa, qb, sa, sb)
+            gather["fused"] = fused_gather(args, wl, operands, C, full, world, rank, dev, stream, flops)
         del full
     value = world * flops / (ms * 1e-3) / 1e12
 
