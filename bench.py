@@ -66,15 +66,34 @@ def profile_traffic(name: str):
     return None
 
 
-class ClockSampler:
-    """SM clock and clock-event (throttle) reasons polled through NVML every 10 ms from
-    start() to stop(), i.e. across the timed region."""
+def nvml_handle_for_cuda_device(nv, cuda_index: int):
+    """The NVML handle of CUDA device `cuda_index`. NVML enumerates every GPU of the machine
+    while CUDA sees only the visible ones (CUDA_VISIBLE_DEVICES), so an NVML index can name
+    another job's GPU; the UUID identifies the same device in both."""
+    import torch
 
-    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4}
+    uuid = str(torch.cuda.get_device_properties(cuda_index).uuid)
+    if not uuid.startswith("GPU-"):
+        uuid = "GPU-" + uuid
+    return nv.nvmlDeviceGetHandleByUUID(uuid)
+
+
+class ClockSampler:
+    """SM clock, clock-event (throttle) reasons and board power polled through NVML every 10 ms.
+
+    NVML's clock and power telemetry trails the GPU by roughly 0.1-0.15 s (measured here: a
+    GEMM loop started at t = 0 shows its power-capped clock from t = 0.15 s on), so the samples
+    that describe a timed region are those taken LAG_S later: stop() keeps polling until the end
+    of the region + LAG_S and reports the window [start + LAG_S, end + LAG_S]."""
+
+    REASONS = {"gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4, "hw_slowdown": 0x8,
+               "sync_boost": 0x10, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+               "hw_power_brake_slowdown": 0x80, "display_clock_setting": 0x100}
+    LAG_S = 0.15
 
     def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.samples: list[tuple[float, int]] = []
+        self.gpu = gpu_index  # CUDA device ordinal (NVML numbers GPUs differently: matched by UUID)
+        self.samples: list[tuple[float, float, int, float]] = []  # (time, SM MHz, reason bits, board W)
         self.smax = 0.0
         self._stop = threading.Event()
         self.t = None
@@ -85,7 +104,7 @@ class ClockSampler:
             import pynvml as nv
 
             nv.nvmlInit()
-            h = nv.nvmlDeviceGetHandleByIndex(self.gpu)
+            h = nvml_handle_for_cuda_device(nv, self.gpu)
             self.smax = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
         except Exception:
             return
@@ -96,7 +115,8 @@ class ClockSampler:
                 try:
                     clk = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
                     rs = int(nv.nvmlDeviceGetCurrentClocksEventReasons(h))
-                    self.samples.append((clk, rs))
+                    pw = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
+                    self.samples.append((time.monotonic(), clk, rs, pw))
                 except Exception:
                     pass
                 self._stop.wait(0.01)
@@ -104,23 +124,28 @@ class ClockSampler:
         self.t = threading.Thread(target=poll, daemon=True)
         self.t.start()
 
-    def mark(self):
-        """Index of the next sample (to select the samples of a sub-interval)."""
-        return len(self.samples)
+    def mark(self) -> float:
+        """Start of a timed region (call right before it)."""
+        return time.monotonic()
 
-    def stop(self, since: int = 0):
+    def stop(self, since: float):
+        """End of the timed region: the lag-shifted window's median clock, reasons and power."""
         if not self.ok:
             return None
+        end = time.monotonic()
+        time.sleep(self.LAG_S + 0.03)
         self._stop.set()
         self.t.join(timeout=2)
-        sm = [c for c, _ in self.samples[since:]]
-        if not sm:
-            sm = [c for c, _ in self.samples]
-        reasons = sorted({n for _, r in self.samples[since:] for n, bit in self.REASONS.items() if r & bit})
-        if not sm:
+        window = [x for x in self.samples if since + self.LAG_S <= x[0] <= end + self.LAG_S]
+        if len(window) < 3:  # a region shorter than a few polls: take everything it may cover
+            window = [x for x in self.samples if since <= x[0] <= end + self.LAG_S]
+        if not window:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": self.smax, "reasons": reasons,
-                "samples": len(self.samples) - since, "source": "NVML, 10 ms polling during the timed region"}
+        reasons = sorted({n for _, _, r, _ in window for n, bit in self.REASONS.items() if r & bit})
+        return {"sm_mhz": statistics.median(c for _, c, _, _ in window), "sm_max_mhz": self.smax,
+                "reasons": reasons, "power_w": round(statistics.median(w for _, _, _, w in window), 1),
+                "samples": len(window), "region_s": round(end - since, 3),
+                "source": f"NVML (device matched by UUID), 10 ms polls shifted by the {self.LAG_S} s telemetry lag"}
 
 
 def dist_setup(args):
