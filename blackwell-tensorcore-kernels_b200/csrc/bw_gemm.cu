@@ -5,6 +5,7 @@
 #include "bw_gemm_kernel.cuh"
 #include "bw_gemm_pair.cuh"
 #include "bw_gemm_pair_mx.cuh"
+#include "bw_gemm_pair_wide.cuh"
 #include "bw_runtime.cuh"
 
 namespace bw {
@@ -103,6 +104,45 @@ bool use_pair(int M, int N, const DeviceState& d) {
   if (forced == 1) return true;
   const long tiles = static_cast<long>((M + 255) / 256) * ((N + 255) / 256);
   return tiles >= d.sms / 4;  // e.g. 2048^3 (64 tiles): pair 828 vs single-CTA 691 TFLOP/s
+}
+
+// 256 x 512 tiles (bw_gemm_pair_wide.cuh): less L2 -> SM traffic per FLOP than 256 x 256.
+template <Kind KIND, bool B_MN, Out OUT>
+int launch_pair_wide(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p, cudaStream_t stream,
+                     const DeviceState& d) {
+  auto kern = bw_tc_gemm_pair_wide_kernel<KIND, B_MN, OUT>;
+  static bool attr_done[64] = {};
+  static int max_clusters[64] = {};
+  int dev = 0;
+  BW_CUDA(cudaGetDevice(&dev));
+  if (!attr_done[dev & 63]) {
+    BW_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, WideCfg::kSmemBytes));
+    attr_done[dev & 63] = true;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (d.sms / 2), 1, 1);
+    cfg.blockDim = dim3(kWideThreads, 1, 1);
+    cfg.dynamicSmemBytes = WideCfg::kSmemBytes;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = d.sms / 2;
+    }
+    max_clusters[dev & 63] = n;
+  }
+  const int tiles = ((p.M + 255) / 256) * ((p.N + 511) / 512);
+  const int resident = max_clusters[dev & 63];
+  const int clusters = tiles < resident ? tiles : resident;
+  p.trace = nullptr;
+  kern<<<2 * clusters, kWideThreads, WideCfg::kSmemBytes, stream>>>(ta, tb, p);
+  BW_CUDA(cudaGetLastError());
+  return BW_OK;
 }
 
 template <Out OUT, int TN>
@@ -332,6 +372,10 @@ int gemm_f16_impl(const void* A, const void* B, float* C, int M, int N, int K, c
   }
   if (pair) {
     if (direct_epilogue_ok(C, N, 4)) {
+      if (env_int("BW_WIDE", 0) != 0) {
+        if (b_mn) return launch_pair_wide<Kind::F16, true, Out::F32>(ta, tb, p, s, *d);
+        return launch_pair_wide<Kind::F16, false, Out::F32>(ta, tb, p, s, *d);
+      }
       if (b_mn) return launch_pair<Kind::F16, true, 3, Out::F32, true, 2>(ta, tb, tc, p, s, *d);
       return launch_pair<Kind::F16, false, 3, Out::F32, true, 2>(ta, tb, tc, p, s, *d);
     }
@@ -386,6 +430,10 @@ int gemm_fp8_impl(const uint8_t* A, const uint8_t* Bt, const float* sa, const fl
   }
   if (pair) {
     const bool direct = direct_epilogue_ok(C, N, static_cast<int>(out_elem_bytes(out_dtype)));
+    if (direct && env_int("BW_WIDE", 0) != 0) {
+      if (out_dtype == BW_OUT_F32) return launch_pair_wide<Kind::F8, false, Out::F32>(ta, tb, p, s, *d);
+      return launch_pair_wide<Kind::F8, false, Out::BF16>(ta, tb, p, s, *d);
+    }
     if (out_dtype == BW_OUT_F32) {
       if (direct) return launch_pair<Kind::F8, false, 3, Out::F32, true, 2>(ta, tb, tc, p, s, *d);
       return launch_pair<Kind::F8, false, 3, Out::F32, false, 2>(ta, tb, tc, p, s, *d);

@@ -46,11 +46,12 @@ def _t(x, dev):
 
 
 SHAPES = [(129, 136, 72), (300, 520, 1000), (1000, 1032, 256), (77, 2056, 528)]
-ENVS = [{}, {"BW_PAIR": "1"}, {"BW_PAIR": "1", "BW_EPI_DIRECT": "0"}, {"BW_PAIR": "0"}, {"BW_SPLITK": "3"}]
+ENVS = [{}, {"BW_PAIR": "1"}, {"BW_PAIR": "1", "BW_EPI_DIRECT": "0"}, {"BW_PAIR": "0"}, {"BW_SPLITK": "3"},
+        {"BW_PAIR": "1", "BW_WIDE": "1"}]
 
 
 @pytest.mark.parametrize("M,N,K", SHAPES)
-@pytest.mark.parametrize("env", ENVS, ids=["auto", "pair", "pair_staged", "single", "splitk"])
+@pytest.mark.parametrize("env", ENVS, ids=["auto", "pair", "pair_staged", "single", "splitk", "pair_wide"])
 def test_f16_writes_stay_inside_c(cuda_dev, monkeypatch, M, N, K, env):
     import torch
 
@@ -67,7 +68,7 @@ def test_f16_writes_stay_inside_c(cuda_dev, monkeypatch, M, N, K, env):
 
 @pytest.mark.parametrize("M,N,K", [(129, 136, 96), (300, 528, 1024), (1000, 1040, 256)])
 @pytest.mark.parametrize("out", [bwgemm.OUT_F32, bwgemm.OUT_BF16])
-@pytest.mark.parametrize("env", ENVS, ids=["auto", "pair", "pair_staged", "single", "splitk"])
+@pytest.mark.parametrize("env", ENVS, ids=["auto", "pair", "pair_staged", "single", "splitk", "pair_wide"])
 def test_fp8_writes_stay_inside_c(cuda_dev, monkeypatch, M, N, K, out, env):
     import torch
 

@@ -424,6 +424,39 @@ def test_splitk_bf16_workspace_per_stream(cuda_dev):
     assert np.abs(_np(C) - R).max() <= o.lowp_tolerance(K, 448 * rsa, 448 * rsb, np.abs(R).max(), True)
 
 
+@pytest.mark.parametrize("M,N,K", [(512, 1024, 512), (300, 1040, 320), (256, 512, 64), (1024, 2064, 1024)])
+@pytest.mark.parametrize("kind", ["f16", "fp8_f32", "fp8_bf16"])
+def test_wide_pair_kernel_parity(cuda_dev, monkeypatch, M, N, K, kind):
+    """The 256 x 512 CTA-pair kernel (two N halves released separately) against the oracle,
+    ragged M / N / K edges included."""
+    import torch
+
+    monkeypatch.setenv("BW_PAIR", "1")
+    monkeypatch.setenv("BW_WIDE", "1")
+    if kind == "f16":
+        A = _f16(o.seeded_uniform((M, K), 111))
+        B = _f16(o.seeded_uniform((K, N), 112))
+        C = _np(bwgemm.gemm_f16(_t(A, cuda_dev).half(), _t(B, cuda_dev).half()))
+        torch.cuda.synchronize()
+        _status_ok()
+        tol = o.f16_tolerance(K, np.abs(A).max(), np.abs(B).max())
+        assert np.abs(C - o.gemm_f64(A, B)).max() <= tol
+        return
+    out = bwgemm.OUT_F32 if kind == "fp8_f32" else bwgemm.OUT_BF16
+    A = o.seeded_normal((M, K), 113)
+    B = o.seeded_normal((K, N), 114)
+    qa, sa = bwgemm.quantize_fp8(_t(A, cuda_dev), False, bwgemm.SCALE_AMAX)
+    qb, sb = bwgemm.quantize_fp8(_t(B, cuda_dev), True, bwgemm.SCALE_AMAX)
+    C = _np(bwgemm.gemm_fp8(qa, qb, sa, sb, out_dtype=out))
+    torch.cuda.synchronize()
+    _status_ok()
+    ra, rsa = o.quant_fp8(A, False, o.SCALE_AMAX)
+    rb, rsb = o.quant_fp8(B, True, o.SCALE_AMAX)
+    R = o.gemm_f64(o.dequant_fp8(ra), o.dequant_fp8(rb), b_trans=True) * float(np.float32(rsa) * np.float32(rsb))
+    tol = o.lowp_tolerance(K, 448 * rsa, 448 * rsb, np.abs(R).max(), out == bwgemm.OUT_BF16)
+    assert np.abs(C - R).max() <= tol
+
+
 @pytest.mark.parametrize("N", [520, 1032])
 def test_fp8_pair_bf16_out_with_unaligned_row_pitch(cuda_dev, monkeypatch, N):
     """N % 16 == 8 makes BF16 rows 16- but not 32-byte aligned: the pair kernel must take the
