@@ -10,9 +10,10 @@
 //
 // Tensor Memory holds one 512-column accumulator (the two halves side by side), so the epilogue
 // cannot run behind a second buffer. Instead each half is released on its own: 8 epilogue warps
-// (two per TMEM lane quarter, 128 columns each) drain half 0 into registers, free it
-// (half_free[0]), store it, then drain and free half 1. The MMA thread starts the next tile's
-// half-0 MMAs as soon as half 0 is free and waits for half 1 only before its first half-1 MMA.
+// (two per TMEM lane quarter, 128 columns each) drain half 0 into registers as soon as its last
+// MMAs complete (accfull[0], committed before the last half-1 MMAs), free it (half_free[0]),
+// store it, then drain and free half 1. The MMA thread starts the next tile's half-0 MMAs as
+// soon as half 0 is free and waits for half 1 only before its first half-1 MMA.
 // Stage = one K atom (A 16 KB + B 2 x 16 KB), 4 stages, 8 MMAs per stage.
 #pragma once
 #include "bw_gemm_kernel.cuh"
@@ -27,8 +28,8 @@ struct WideCfg {
   static constexpr int kBHalfBytes = 128 * kSlabBytes;  // this CTA's 128 columns of one N half
   static constexpr int kStageBytes = kABytes + 2 * kBHalfBytes;
   static constexpr int kBarOffset = kWideStages * kStageBytes;
-  // full[S], empty[S], accfull, half_free[2], teardown
-  static constexpr int kNumBars = 2 * kWideStages + 4;
+  // full[S], empty[S], accfull[2], half_free[2], teardown
+  static constexpr int kNumBars = 2 * kWideStages + 5;
   static constexpr int kSmemBytes = kBarOffset + kNumBars * 8 + 16 + 1024;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
   static constexpr int kTmemCols = 512;
@@ -48,9 +49,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kBarOffset);
   uint64_t* full = bars;
   uint64_t* empty = bars + kWideStages;
-  uint64_t* accfull = bars + 2 * kWideStages;
-  uint64_t* half_free = accfull + 1;  // [2], on the leader: both CTAs' 8 epilogue warps arrive
-  uint64_t* teardown = accfull + 3;
+  uint64_t* accfull = bars + 2 * kWideStages;  // [2]: N half h of the tile is complete
+  uint64_t* half_free = accfull + 2;  // [2], on the leader: both CTAs' 8 epilogue warps arrive
+  uint64_t* teardown = accfull + 4;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -69,8 +70,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kWideStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-    mbar_init(accfull, 1);
-    for (int h = 0; h < 2; ++h) mbar_init(&half_free[h], 2 * 8);
+    for (int h = 0; h < 2; ++h) {
+      mbar_init(&accfull[h], 1);
+      mbar_init(&half_free[h], 2 * 8);
+    }
     mbar_init(teardown, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -151,15 +154,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
               if constexpr (KIND == Kind::F16) umma_f16_pair(d_tmem, adesc, bdesc, idesc, acc);
               else umma_f8f6f4_pair(d_tmem, adesc, bdesc, idesc, acc);
             }
+            if (kb == nk - 1) {  // half h of the tile is final: its epilogue may start now
+              umma_commit_pair(accfull_own + h * 8);
+              umma_commit_pair(accfull_peer + h * 8);
+            }
           }
           if (!ok) break;
           umma_commit_pair(empty_own + s * 8);
           umma_commit_pair(empty_peer + s * 8);
           if (++s == kWideStages) { s = 0; ph ^= 1; }
-        }
-        if (ok) {
-          umma_commit_pair(accfull_own);
-          umma_commit_pair(accfull_peer);
         }
       }
       umma_commit_pair(smem_u32(teardown));
@@ -177,11 +180,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
     for (int t = cluster; t < num_tiles; t += nclusters, ++local) {
       int tm, tn;
       tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
-      if (!mbar_wait(accfull, static_cast<uint32_t>(local & 1), wc, 55)) break;
-      tc_fence_after();
       const int row = tm * TM + static_cast<int>(rank) * 128 + q * 32 + lane;
+      bool ok = true;
 #pragma unroll 1
       for (int h = 0; h < 2; ++h) {
+        if (!mbar_wait(&accfull[h], static_cast<uint32_t>(local & 1), wc, 55)) { ok = false; break; }
+        tc_fence_after();
         const int cols = 256 * h + 128 * cpart;
         uint32_t r[128];
         const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + cols;
@@ -219,6 +223,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
           }
         }
       }
+      if (!ok) break;
     }
   }
 
