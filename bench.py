@@ -545,7 +545,7 @@ def compare_rows(args, wl, inp, dev, stream):
             e8b = sfb.view(torch.float8_e8m0fnu)
             interleaved("ours_mxfp4_bf16out_tflops",
                         lambda: bwgemm.gemm_mxfp4(q4a, q4b, sfa, sfb, K, C=C8, stream=stream),
-                        "cublaslt_mxfp4_bf16out_tflops",
+                        "torch_cutlass_mxfp4_bf16out_tflops",  # torch scaled_mm runs a CUTLASS kernel for MXFP4
                         lambda: F.scaled_mm(a4, b4, e8a, F.ScalingType.BlockWise1x32, e8b,
                                             F.ScalingType.BlockWise1x32, swizzle_a=F.SwizzleType.SWIZZLE_32_4_4,
                                             swizzle_b=F.SwizzleType.SWIZZLE_32_4_4, output_dtype=torch.bfloat16))

@@ -6,7 +6,8 @@
 //   cublas_tc         cublasGemmEx FP16 in, FP32 compute and out
 //   cublaslt_fp8      cublasLtMatmul E4M3 "TN", FP32 out, no scales
 //   cublaslt_fp8_amax cublasLtMatmul E4M3 with per-tensor scale pointers (amax/448), BF16 out
-//   cublaslt_mxfp4    cublasLtMatmul E2M1 with VEC32_UE8M0 block scales, BF16 out
+//   cublaslt_mxfp4    cublasLtMatmul E2M1 with VEC32_UE8M0 block scales, BF16 out (cuBLASLt 12.9.1
+//                     rejects this combination of precisions; the row then reports unavailable)
 #include <cublasLt.h>
 #include <cublas_v2.h>
 #include <cuda_bf16.h>

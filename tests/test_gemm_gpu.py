@@ -480,10 +480,12 @@ def test_fp8_pair_bf16_out_with_unaligned_row_pitch(cuda_dev, monkeypatch, N):
 
 
 @pytest.mark.parametrize("M,N,K", [(1024, 1024, 1024), (4096, 4096, 2048)])
-def test_mxfp4_bit_identical_to_cublaslt(cuda_dev, M, N, K):
-    """Independent check of the block-scaled path: cuBLASLt's MXFP4 GEMM (through
-    torch.nn.functional.scaled_mm, BlockWise1x32 with the 32x4x4-swizzled UE8M0 layout, which
-    is our scale-factor layout) on the very same quantised buffers gives the same BF16 bits."""
+def test_mxfp4_bit_identical_to_library(cuda_dev, M, N, K):
+    """Independent check of the block-scaled path: the library MXFP4 GEMM that
+    torch.nn.functional.scaled_mm runs (BlockWise1x32 with the 32x4x4-swizzled UE8M0 layout,
+    which is our scale-factor layout; a CUTLASS kernel in this torch build - cuBLASLt 12.9
+    rejects the E2M1 / VEC32_UE8M0 / BF16 combination) on the very same quantised buffers gives
+    the same BF16 bits."""
     import torch
 
     F = torch.nn.functional
