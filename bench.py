@@ -324,6 +324,20 @@ def make_inputs(workload: str, rank: int, dev):  # noqa: C901
     return {"A32": A32, "B32": B32}
 
 
+def cpu_model() -> str:
+    """The host CPU's model name (first /proc/cpuinfo entry) and its logical CPU count."""
+    name = "unknown CPU"
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    name = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return f"{name}, {os.cpu_count()} logical CPUs"
+
+
 def cpu_baseline(threads: int, budget_s: float = 12.0):
     """FP64 oracle GEMM (oracle/bw_oracle.c) on host cores over a bounded row sample of the
     8192^3 FP16 workload; returns TFLOP/s and the sample description."""
@@ -489,7 +503,7 @@ def run_ours(args, world, rank, local):
         threads = os.cpu_count() or 1
         v, sample = cpu_baseline(threads)
         line["cpu_baseline"] = {"value": round(v, 5), "unit": "TFLOP/s", "cores": threads, "kind": "port",
-                                "sample": sample}
+                                "sample": sample, "cpu": cpu_model()}
     return line
 
 
