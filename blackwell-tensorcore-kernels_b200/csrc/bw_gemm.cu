@@ -39,6 +39,29 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, 
   return BW_OK;
 }
 
+// Co-resident CTA pairs of a persistent `__cluster_dims__(2,1,1)` kernel (clusters must fit
+// inside one GPC, so this can be below sms / 2); falls back to sms / 2 if the query fails.
+template <typename Kernel>
+int pair_clusters_resident(Kernel kern, int threads, int smem_bytes, const DeviceState& d) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * (d.sms / 2), 1, 1);
+  cfg.blockDim = dim3(threads, 1, 1);
+  cfg.dynamicSmemBytes = smem_bytes;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = 2;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    n = d.sms / 2;
+  }
+  return n;
+}
+
 template <Kind KIND, bool B_MN, int STAGES, Out OUT, bool DIRECT_EPI, int KSUB, int TN = 256>
 int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, GemmParams p,
                 cudaStream_t stream, const DeviceState& d, const PeerMaps* pm = nullptr) {
@@ -56,23 +79,7 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
   // GPC, so this can be below sms/2).
   static int max_clusters[64] = {};
   if (max_clusters[dev & 63] == 0) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(2 * (d.sms / 2), 1, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
-    cfg.dynamicSmemBytes = Cfg::kSmemBytes;
-    cudaLaunchAttribute attr;
-    attr.id = cudaLaunchAttributeClusterDimension;
-    attr.val.clusterDim.x = 2;
-    attr.val.clusterDim.y = 1;
-    attr.val.clusterDim.z = 1;
-    cfg.attrs = &attr;
-    cfg.numAttrs = 1;
-    int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
-      cudaGetLastError();
-      n = d.sms / 2;
-    }
-    max_clusters[dev & 63] = n;
+    max_clusters[dev & 63] = pair_clusters_resident(kern, kThreads, Cfg::kSmemBytes, d);
   }
   const int tiles = ((p.M + 255) / 256) * ((p.N + TN - 1) / TN);
   const int resident = max_clusters[dev & 63];
@@ -118,23 +125,7 @@ int launch_pair_wide(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p,
   if (!attr_done[dev & 63]) {
     BW_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, WideCfg::kSmemBytes));
     attr_done[dev & 63] = true;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(2 * (d.sms / 2), 1, 1);
-    cfg.blockDim = dim3(kWideThreads, 1, 1);
-    cfg.dynamicSmemBytes = WideCfg::kSmemBytes;
-    cudaLaunchAttribute attr;
-    attr.id = cudaLaunchAttributeClusterDimension;
-    attr.val.clusterDim.x = 2;
-    attr.val.clusterDim.y = 1;
-    attr.val.clusterDim.z = 1;
-    cfg.attrs = &attr;
-    cfg.numAttrs = 1;
-    int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
-      cudaGetLastError();
-      n = d.sms / 2;
-    }
-    max_clusters[dev & 63] = n;
+    max_clusters[dev & 63] = pair_clusters_resident(kern, kWideThreads, WideCfg::kSmemBytes, d);
   }
   const int tiles = ((p.M + 255) / 256) * ((p.N + 511) / 512);
   const int resident = max_clusters[dev & 63];
@@ -157,23 +148,7 @@ int launch_pair_mx(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorM
   if (!attr_done[dev & 63]) {
     BW_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
     attr_done[dev & 63] = true;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(2 * (d.sms / 2), 1, 1);
-    cfg.blockDim = dim3(kMxThreads, 1, 1);
-    cfg.dynamicSmemBytes = Cfg::kSmemBytes;
-    cudaLaunchAttribute attr;
-    attr.id = cudaLaunchAttributeClusterDimension;
-    attr.val.clusterDim.x = 2;
-    attr.val.clusterDim.y = 1;
-    attr.val.clusterDim.z = 1;
-    cfg.attrs = &attr;
-    cfg.numAttrs = 1;
-    int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
-      cudaGetLastError();
-      n = d.sms / 2;
-    }
-    max_clusters[dev & 63] = n;
+    max_clusters[dev & 63] = pair_clusters_resident(kern, kMxThreads, Cfg::kSmemBytes, d);
   }
   const int tiles = ((p.M + 255) / 256) * ((p.N + TN - 1) / TN);
   const int resident = max_clusters[dev & 63];
