@@ -42,7 +42,8 @@ def _guards_ok(whole, M, N, elem):
     return (w[:GUARD] == 0x5A).all() and (w[GUARD + M * N * elem:] == 0x5A).all()
 
 
-ENVS = [{}, {"BW_PAIR": "1"}, {"BW_PAIR": "0"}, {"BW_SPLITK": "4"}, {"BW_PAIR": "1", "BW_EPI_DIRECT": "0"}]
+ENVS = [{}, {"BW_PAIR": "1"}, {"BW_PAIR": "0"}, {"BW_SPLITK": "4"}, {"BW_PAIR": "1", "BW_EPI_DIRECT": "0"},
+        {"BW_PAIR": "1", "BW_WIDE": "1"}]
 
 
 @pytest.mark.parametrize("case", range(12))
