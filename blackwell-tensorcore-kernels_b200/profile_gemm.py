@@ -1,5 +1,8 @@
 """Small driver for profiling one GEMM kind under ncu: KIND=f16|fp8|fp4|mxfp4, N=size (square).
-Runs the GEMM three times (ncu -s 1 -c 1 then captures the second launch).
+Runs the GEMM three times (ncu -s 1 -c 1 then captures the second launch). KIND=quant instead
+runs three rounds of the quantisers on an N x N FP32 input: MXFP4 rows, MXFP4 columns (the Bt
+operand) and a transposed E4M3 with the fixed scale (ncu -k regex:k_quant -s 3 -c 3 captures
+the second round).
 
     KIND=f16 N=8192 ncu --set full --clock-control none -k regex:bw_tc_gemm -s 1 -c 1 \
         -o prof python blackwell-tensorcore-kernels_b200/profile_gemm.py
@@ -22,6 +25,13 @@ elif kind == 'fp8':
 elif kind == 'fp4':
     qa, sa = bwgemm.quantize_fp4(torch.randn(M, K, device=dev)); qb, sb = bwgemm.quantize_fp4(torch.randn(K, N, device=dev), True)
     C = torch.empty(M, N, device=dev, dtype=torch.bfloat16); f = lambda: bwgemm.gemm_fp4(qa, qb, K, sa, sb, C=C)
+elif kind == 'quant':
+    x = torch.randn(M, K, device=dev)
+
+    def f():
+        bwgemm.quantize_mxfp4(x, False)
+        bwgemm.quantize_mxfp4(x, True)
+        bwgemm.quantize_fp8(x, True, bwgemm.SCALE_FIXED8)
 else:
     qa, sfa = bwgemm.quantize_mxfp4(torch.randn(M, K, device=dev)); qb, sfb = bwgemm.quantize_mxfp4(torch.randn(K, N, device=dev), True)
     C = torch.empty(M, N, device=dev, dtype=torch.bfloat16); f = lambda: bwgemm.gemm_mxfp4(qa, qb, sfa, sfb, K, C=C)
