@@ -74,6 +74,7 @@ def lib():
         "bw_shutdown": [],
         "bw_version": [],
         "bw_num_sms": [I],
+        "bw_device_state_ready": [I],
         "bw_device_status": [P, P],
         "bw_set_wait_budget_ns": [ctypes.c_ulonglong],
         "bw_set_trace_buffer": [P, I],

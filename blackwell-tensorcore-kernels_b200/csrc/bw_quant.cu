@@ -9,6 +9,7 @@
 //   packed fp4: element 2i in the low nibble              (src/gemm_mma_fp8.cu:70-80)
 // New behaviour (no reference counterpart): per-tensor amax scaling and UE8M0 block-32
 // scales (e = floor(log2(block amax)) - 2).
+#include <atomic>
 #include <cuda_fp16.h>
 #include <cuda_fp8.h>
 
@@ -159,6 +160,10 @@ __global__ void k_quant_rowmajor(const float* __restrict__ src, uint8_t* __restr
 // consecutive codes of one dst row and stores them as one 16-byte (8 packed bytes for FMT 2)
 // store when rows % 16 == 0 and dst is aligned; byte stores otherwise.
 constexpr int kQuantColsRows = 128;
+inline unsigned transpose_grid_y(int rows) {
+  const long long g = (static_cast<long long>(rows) + kQuantColsRows - 1) / kQuantColsRows;
+  return static_cast<unsigned>(g < 65535 ? g : 65535);
+}
 template <int FMT>
 __global__ void __launch_bounds__(256) k_quant_transpose(const float* __restrict__ src, uint8_t* __restrict__ dst,
                                                          int rows, int cols, int mode, float qmax,
@@ -167,27 +172,32 @@ __global__ void __launch_bounds__(256) k_quant_transpose(const float* __restrict
   tensor_scale(mode, amax_bits, qmax, mul, s);
   if (scale_out && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) *scale_out = s;
   const int c = blockIdx.x * 32 + (threadIdx.x & 31);
-  const int r0 = blockIdx.y * kQuantColsRows + 16 * (threadIdx.x >> 5);
-  if (c >= cols || r0 >= rows) return;
-  float v[16];
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = (r0 + i < rows) ? __ldcs(src + static_cast<size_t>(r0 + i) * cols + c) : 0.f;
+  if (c >= cols) return;
   const bool vec = rows % 16 == 0 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0;
-  uint32_t w[4];
-  encode16<FMT>(v, mul, w);
-  if constexpr (FMT == 2) {
-    uint8_t* row = dst + static_cast<size_t>(c) * (rows / 2);
-    if (vec) {
-      *reinterpret_cast<uint2*>(row + r0 / 2) = make_uint2(w[0], w[1]);
+  // grid.y is capped at 65535: row groups beyond it are walked by a grid-stride loop
+  for (long long rb = blockIdx.y; rb * kQuantColsRows < rows; rb += gridDim.y) {
+    const int r0 = static_cast<int>(rb * kQuantColsRows) + 16 * (threadIdx.x >> 5);
+    if (r0 >= rows) continue;
+    float v[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = (r0 + i < rows) ? __ldcs(src + static_cast<size_t>(r0 + i) * cols + c) : 0.f;
+    uint32_t w[4];
+    encode16<FMT>(v, mul, w);
+    if constexpr (FMT == 2) {
+      uint8_t* row = dst + static_cast<size_t>(c) * (rows / 2);
+      if (vec) {
+        *reinterpret_cast<uint2*>(row + r0 / 2) = make_uint2(w[0], w[1]);
+      } else {
+        for (int i = 0; i < 16 && r0 + i < rows; i += 2)
+          row[(r0 + i) / 2] = static_cast<uint8_t>(w[i / 8] >> (4 * (i % 8)));
+      }
     } else {
-      for (int i = 0; i < 16 && r0 + i < rows; i += 2) row[(r0 + i) / 2] = static_cast<uint8_t>(w[i / 8] >> (4 * (i % 8)));
-    }
-  } else {
-    uint8_t* row = dst + static_cast<size_t>(c) * rows;
-    if (vec) {
-      *reinterpret_cast<uint4*>(row + r0) = make_uint4(w[0], w[1], w[2], w[3]);
-    } else {
-      for (int i = 0; i < 16 && r0 + i < rows; ++i) row[r0 + i] = static_cast<uint8_t>(w[i / 4] >> (8 * (i % 4)));
+      uint8_t* row = dst + static_cast<size_t>(c) * rows;
+      if (vec) {
+        *reinterpret_cast<uint4*>(row + r0) = make_uint4(w[0], w[1], w[2], w[3]);
+      } else {
+        for (int i = 0; i < 16 && r0 + i < rows; ++i) row[r0 + i] = static_cast<uint8_t>(w[i / 4] >> (8 * (i % 4)));
+      }
     }
   }
 }
@@ -386,7 +396,7 @@ int quant_tensor(const float* src, uint8_t* dst, float* scale_out, int rows, int
     BW_CUDA(cudaGetLastError());
   }
   if (transpose) {
-    dim3 grid((cols + 31) / 32, (rows + kQuantColsRows - 1) / kQuantColsRows);
+    dim3 grid((cols + 31) / 32, transpose_grid_y(rows));
     k_quant_transpose<FMT><<<grid, 256, 0, s>>>(src, dst, rows, cols, mode, qmax, amax, scale_out);
   } else {
     k_quant_rowmajor<FMT><<<grid_for(FMT == 2 ? n / 2 : n, *d), kQThreads, 0, s>>>(src, dst, rows, cols, mode, qmax,
@@ -451,6 +461,8 @@ int bw_quantize_mxfp4(const float* src, uint8_t* dst, uint8_t* sf, int rows, int
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   BW_CUDA(cudaMemsetAsync(sf, 0x7f, bw_sf_bytes(outer, K), s));
   if (transpose) {
+    if ((K + 255) / 256 > 65535)
+      return set_error(BW_ERR_INVALID, "mxfp4 transposed: K = %d exceeds the %d rows one launch covers", K, 65535 * 256);
     dim3 grid((outer + 31) / 32, (K + 255) / 256);
     k_quant_mx_cols<<<grid, 256, 0, s>>>(src, dst, sf, K, outer, mode);
   } else {
@@ -500,10 +512,13 @@ int unshard_elems(const void* src, void* dst, int M, int N, int world, int elem_
 
 // =========================================================================================
 // bw_quantize_fp8_noalloc: the per-tensor E4M3 quantiser for callers that cannot allocate
-// device memory. Some callers are not allowed to call cudaMalloc at all: code running in a
-// stream callback (CUDA forbids runtime API calls there), plugins hosted by a framework whose
-// own allocator has already reserved the device memory and must account for every byte, and
-// serving loops with a no-allocation latency contract. bw_quantize_fp8 needs a small device
+// device memory. Some callers are not allowed to call cudaMalloc at all: plugins hosted by a
+// framework whose own allocator has already reserved the device memory and must account for
+// every byte, and serving loops with a no-allocation latency contract (a cudaMalloc can
+// synchronise the device and take milliseconds). It still calls the CUDA runtime (kernel
+// launches, and a symbol lookup on first use), so it must be called from an ordinary host
+// thread, never from a host function or stream callback (CUDA forbids runtime calls there);
+// a callback-driven design enqueues it from the thread that owns the stream. bw_quantize_fp8 needs a small device
 // workspace for its amax reduction, which the library cudaMallocs on a device's first use;
 // this variant keeps that scratch in a fixed array compiled into the library instead.
 //
@@ -528,8 +543,11 @@ constexpr int kNoAllocAmaxBlocks = 16384;
 constexpr int kNoAllocChunk = 8192;  // elements reduced by one block (32 per thread)
 static __device__ __align__(256) unsigned g_noalloc_amax_scratch[kNoAllocAmaxBlocks + 1];
 
-void* g_noalloc_scratch_addr[64] = {};
-int g_noalloc_sms[64] = {};
+// Per-device cache of the set-up results. Two host threads making their first call on one
+// device may both run the set-up; they store the same values, published with release order
+// (the SM count before the address, so a thread that sees the address also sees the count).
+std::atomic<void*> g_noalloc_scratch_addr[64] = {};
+std::atomic<int> g_noalloc_sms[64] = {};
 
 __global__ void k_amax_partial(const float* __restrict__ src, long long n, unsigned* __restrict__ partial) {
   const long long base = static_cast<long long>(blockIdx.x) * kNoAllocChunk;
@@ -569,17 +587,19 @@ __global__ void k_store_one(float* out) { *out = 1.f; }
 // count (neither call allocates).
 int noalloc_setup(int dev, unsigned** scratch, int* sms) {
   if (dev < 0 || dev >= 64) return set_error(BW_ERR_INVALID, "device index %d out of range", dev);
-  if (!g_noalloc_scratch_addr[dev]) {
+  void* addr = g_noalloc_scratch_addr[dev].load(std::memory_order_acquire);
+  if (!addr) {
     void* ptr = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_amax_scratch);
     if (e != cudaSuccess || !ptr) return cuda_error(e, "cudaGetSymbolAddress(no-alloc scratch)");
     int n = 0;
     BW_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
-    g_noalloc_sms[dev] = n > 0 ? n : 1;
-    g_noalloc_scratch_addr[dev] = ptr;
+    g_noalloc_sms[dev].store(n > 0 ? n : 1, std::memory_order_relaxed);
+    g_noalloc_scratch_addr[dev].store(ptr, std::memory_order_release);
+    addr = ptr;
   }
-  *scratch = static_cast<unsigned*>(g_noalloc_scratch_addr[dev]);
-  *sms = g_noalloc_sms[dev];
+  *scratch = static_cast<unsigned*>(addr);
+  *sms = g_noalloc_sms[dev].load(std::memory_order_relaxed);
   return BW_OK;
 }
 
@@ -623,7 +643,7 @@ extern "C" int bw_quantize_fp8_noalloc(const float* src, uint8_t* dst, float* sc
     BW_CUDA(cudaGetLastError());
   }
   if (transpose) {
-    dim3 grid((cols + 31) / 32, (rows + kQuantColsRows - 1) / kQuantColsRows);
+    dim3 grid((cols + 31) / 32, transpose_grid_y(rows));
     k_quant_transpose<0><<<grid, 256, 0, s>>>(src, dst, rows, cols, scale_mode, 448.f, amax, scale_out);
   } else {
     long long g = (n + kQThreads - 1) / kQThreads;

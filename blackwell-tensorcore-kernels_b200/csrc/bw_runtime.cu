@@ -175,6 +175,11 @@ int bw_num_sms(int device) {
   return n;
 }
 
+int bw_device_state_ready(int device) {
+  if (device < 0 || device >= kMaxDevices) return 0;
+  return g_dev[device].ready ? 1 : 0;
+}
+
 int bw_shutdown(void) {
   std::lock_guard<std::mutex> lk(g_mu);
   int cur = 0;

@@ -65,6 +65,10 @@ int bw_shutdown(void);                /* free library-owned device memory on all
 const char* bw_last_error_string(void);
 int bw_version(void);                 /* (major << 16) | minor */
 int bw_num_sms(int device);
+/* Diagnostic: 1 when the library has set up its state on `device` (status word and the
+ * small workspace it cudaMallocs on a device's first use), else 0; allocates nothing and
+ * makes no CUDA call. */
+int bw_device_state_ready(int device);
 /* Reads (after synchronising `stream`) and clears the device status word that kernels
  * set when a bounded wait expires: 0 = ok, else (BW_ERR_TIMEOUT << 8) | site. */
 int bw_device_status(void* stream, int* out_status);
@@ -125,15 +129,16 @@ int bw_quantize_fp8(const float* src, uint8_t* dst, float* scale_out, int rows, 
 int bw_quantize_fp4(const float* src, uint8_t* dst, float* scale_out, int rows, int cols, int transpose,
                     int scale_mode, int container, void* stream);
 /* bw_quantize_fp8 for callers that cannot allocate device memory (no counterpart in the
- * reference). Stream callbacks may not call the CUDA runtime, framework-hosted plugins may
- * find the device memory already reserved by the host's own allocator, and latency-bound
- * serving loops may forbid allocation; bw_quantize_fp8 needs a small library-allocated
+ * reference). Framework-hosted plugins may find the device memory already reserved by the
+ * host's own allocator, and latency-bound serving loops may forbid allocation; bw_quantize_fp8 needs a small library-allocated
  * workspace for its amax reduction, this variant uses a fixed scratch array compiled into the
  * library (64 KiB per device, held until exit) and calls no allocating routine. Same
  * arguments and bit-identical results. Limit: rows * cols <= 134,217,728 elements, larger
  * inputs return BW_ERR_INVALID. The first call on each device looks the array up (make it
  * outside any stream capture). Calls share the array: calls that may overlap on the GPU
- * (unordered streams) race and must be serialised by the caller. */
+ * (unordered streams) race and must be serialised by the caller. It launches kernels, so call
+ * it from an ordinary host thread, not from a host function / stream callback (CUDA forbids
+ * runtime calls there). */
 int bw_quantize_fp8_noalloc(const float* src, uint8_t* dst, float* scale_out, int rows, int cols, int transpose,
                             int scale_mode, void* stream);
 /* Packed E2M1 plus UE8M0 scale factors along the contiguous (K) dimension of dst.

@@ -7,8 +7,10 @@
 # Not built: cutlass_sm90.cu (sm_90a wgmma only), the FP4/MXFP4 paths (sm_120a-only PTX,
 # guarded by BUILD_SM120A), mma_rate_probe.cu (its own binary).
 set -euo pipefail
-REF=${REF:-/root/reference}
 HERE="$(cd "$(dirname "$0")" && pwd)"
+# The reference checkout: BW_REFERENCE_DIR, else a directory named "reference" beside this
+# repository's own directory.
+REF=${BW_REFERENCE_DIR:-$HERE/../../reference}
 OUT="$HERE/_ref"
 [ -d "$REF/src" ] || { echo "reference sources not found at $REF" >&2; exit 1; }
 mkdir -p "$OUT/obj"

@@ -1,6 +1,6 @@
 """The reference-facing driver end to end: gemm_bench with the reference's command line and
 inputs (glibc rand(), uniform[-0.5, 0.5]) must reproduce the reference's committed
-max_abs_err column (results/bench.csv rows at 512^3 and 1024^3 of the reference repo) for our
+max_abs_err column (results/bench.csv rows at 512^3, 1024^3 and 8192^3 of the reference repo) for our
 tcgen05 rows, write the reference's CSV schema, and honour the kernel filter."""
 import csv
 import os
@@ -15,7 +15,8 @@ BIN = os.path.join(REPO, "blackwell-tensorcore-kernels_b200", "gemm_bench")
 
 # reference results/bench.csv: wmma/mma_* (fp16), mma_fp8, mma_fp4, mma_mxfp4
 REF = {512: {"tc_f16": 0.00254, "tc_fp8": 0.283, "tc_fp4": 1.16, "tc_mxfp4": 1.16},
-       1024: {"tc_f16": 0.00376, "tc_fp8": 0.439, "tc_fp4": 1.87, "tc_mxfp4": 1.87}}
+       1024: {"tc_f16": 0.00376, "tc_fp8": 0.439, "tc_fp4": 1.87, "tc_mxfp4": 1.87},
+       8192: {"tc_f16": 0.0112, "tc_fp8": 1.4, "tc_fp4": 5.97, "tc_mxfp4": 5.97}}  # bench.csv:64,69-72
 
 
 def _run(n, tmp_path, kernels):
@@ -28,7 +29,7 @@ def _run(n, tmp_path, kernels):
         return list(csv.DictReader(f)), r.stdout
 
 
-@pytest.mark.parametrize("n", [512, 1024])
+@pytest.mark.parametrize("n", [512, 1024, 8192])
 def test_reference_max_abs_err_column(tmp_path, n):
     rows, _ = _run(n, tmp_path, "tc_f16,tc_fp8,tc_fp4,tc_mxfp4,cublas_tc,cublaslt_fp8")
     got = {r["kernel"]: float(r["max_abs_err"]) for r in rows}
