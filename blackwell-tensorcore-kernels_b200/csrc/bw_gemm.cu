@@ -6,6 +6,7 @@
 #include "bw_gemm_pair.cuh"
 #include "bw_gemm_pair_mx.cuh"
 #include "bw_gemm_pair_wide.cuh"
+#include "bw_gemm_panel.cuh"
 #include "bw_runtime.cuh"
 
 namespace bw {
@@ -237,6 +238,57 @@ bool use_narrow(int M, int N, const DeviceState& d) {
   return tiles256 < d.sms;
 }
 
+// Column-panel kernel (bw_gemm_panel.cuh) for M <= 256: the panel width W that puts every
+// 128-row x W unit on its own SM in one wave (W a multiple of 32, of 64 for an N-major B, at
+// most 512 TMEM columns), or 0 when the kernel does not apply: M > 256, K < 512, C not
+// 32-byte aligned per row (direct stores), W above 512 or below 96, or under 3/4 of the SMs
+// busy.
+// BW_PANEL = 0 disables it, 1 forces it wherever it can run.
+int panel_width(int M, int N, int K, bool gran64, const void* C, int elem, const DeviceState& d) {
+  const int forced = env_int("BW_PANEL", -1);
+  if (forced == 0 || M > 256 || !direct_epilogue_ok(C, N, elem)) return 0;
+  if (forced != 1 && K < 512) return 0;
+  const int gran = gran64 ? 64 : 32;
+  const long tiles_m = (M + 127) / 128;
+  const long want = (static_cast<long>(N) * tiles_m + d.sms - 1) / d.sms;
+  long W = (want + gran - 1) / gran * gran;
+  if (W < gran) W = gran;
+  if (W > kPanelMaxW) return 0;
+  const long units = tiles_m * ((N + W - 1) / W);
+  if (units > d.sms) return 0;
+  // Narrow panels lose: each CTA re-reads all of A (from L2) for W columns of B, so below
+  // ~96 columns the L2 -> SM traffic of A outweighs B (measured: 128 x 8192 x 8192 FP16 at
+  // W = 64 took 47.8 us against 31.9 us split-K; W = 112..448 were 8-38% faster than split-K).
+  if (forced != 1 && (units * 4 < 3L * d.sms || W < 96)) return 0;
+  return static_cast<int>(W);
+}
+
+template <Kind KIND, bool B_MN, Out OUT>
+int launch_panel(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int W, int b_box,
+                 cudaStream_t stream) {
+  auto kern = bw_tc_gemm_panel_kernel<KIND, B_MN, OUT>;
+  constexpr int kMaxSmem = 232448;
+  static bool attr_done[64] = {};
+  int dev = 0;
+  BW_CUDA(cudaGetDevice(&dev));
+  if (!attr_done[dev & 63]) {
+    BW_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem));
+    attr_done[dev & 63] = true;
+  }
+  PanelParams pp;
+  pp.W = W;
+  pp.panels = (p.N + W - 1) / W;
+  pp.stage_bytes = kBM * kSlabBytes + W * kSlabBytes;
+  pp.stages = (kMaxSmem - panel_smem_bytes(0, 0)) / pp.stage_bytes;
+  if (pp.stages > kPanelMaxStages) pp.stages = kPanelMaxStages;
+  if (pp.stages < 2) return set_error(BW_ERR_INVALID, "panel width %d leaves fewer than 2 stages", W);
+  pp.b_box = b_box;
+  const int units = ((p.M + kBM - 1) / kBM) * pp.panels;
+  kern<<<units, kThreads, panel_smem_bytes(pp.stages, pp.stage_bytes), stream>>>(ta, tb, p, pp);
+  BW_CUDA(cudaGetLastError());
+  return BW_OK;
+}
+
 // C (BF16) = workspace (FP32; scales already applied by the split-K epilogue), 8 per thread.
 __global__ void k_f32_to_bf16(const float4* __restrict__ src, uint4* __restrict__ dst, long long n8) {
   const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
@@ -324,6 +376,18 @@ int gemm_f16_impl(const void* A, const void* B, float* C, int M, int N, int K, c
   DeviceState* d;
   if ((r = ensure_device(&d)) != BW_OK) return r;
   if (K == 0) { BW_CUDA(cudaMemsetAsync(C, 0, sizeof(float) * size_t(M) * N, s)); return BW_OK; }
+  if (const int pw = g ? 0 : panel_width(M, N, K, b_mn, C, 4, *d)) {
+    const int box = b_mn ? 64 : (pw <= 256 ? pw : pw / 2);
+    CUtensorMap ta, tb;
+    if ((r = make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, A, K, M, uint64_t(K) * 2, 64, 128)) != BW_OK) return r;
+    if (b_mn) r = make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, B, N, K, uint64_t(N) * 2, 64, 64);
+    else r = make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, B, K, N, uint64_t(K) * 2, 64, box);
+    if (r != BW_OK) return r;
+    GemmParams p = base_params(*d, C, M, N, K);
+    p.hints = env_int("BW_L2_HINTS", 0);
+    if (b_mn) return launch_panel<Kind::F16, true, Out::F32>(ta, tb, p, pw, box, s);
+    return launch_panel<Kind::F16, false, Out::F32>(ta, tb, p, pw, box, s);
+  }
   const int splits = g ? 1 : choose_splits(M, N, (K + 63) / 64, 4, *d);
   const bool pair = g || (splits == 1 && use_pair(M, N, *d));
   const bool narrow = !pair && splits == 1 && use_narrow(M, N, *d);
@@ -381,6 +445,18 @@ int gemm_fp8_impl(const uint8_t* A, const uint8_t* Bt, const float* sa, const fl
   DeviceState* d;
   if ((r = ensure_device(&d)) != BW_OK) return r;
   if (K == 0) { BW_CUDA(cudaMemsetAsync(C, 0, out_elem_bytes(out_dtype) * size_t(M) * N, s)); return BW_OK; }
+  if (const int pw = g ? 0 : panel_width(M, N, K, false, C, static_cast<int>(out_elem_bytes(out_dtype)), *d)) {
+    const int box = pw <= 256 ? pw : pw / 2;
+    CUtensorMap ta, tb;
+    if ((r = make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, A, K, M, uint64_t(K), 128, 128)) != BW_OK) return r;
+    if ((r = make_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, Bt, K, N, uint64_t(K), 128, box)) != BW_OK) return r;
+    GemmParams p = base_params(*d, C, M, N, K);
+    p.hints = env_int("BW_L2_HINTS", 0);
+    p.scale_a = sa;
+    p.scale_b = sb;
+    if (out_dtype == BW_OUT_F32) return launch_panel<Kind::F8, false, Out::F32>(ta, tb, p, pw, box, s);
+    return launch_panel<Kind::F8, false, Out::BF16>(ta, tb, p, pw, box, s);
+  }
   const int splits = g ? 1 : choose_splits(M, N, (K + 127) / 128, static_cast<int>(out_elem_bytes(out_dtype)), *d);
   const bool pair = g || (splits == 1 && use_pair(M, N, *d));
   const bool narrow = !pair && splits == 1 && use_narrow(M, N, *d);

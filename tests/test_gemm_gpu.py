@@ -504,3 +504,37 @@ def test_mxfp4_bit_identical_to_library(cuda_dev, M, N, K):
     torch.cuda.synchronize()
     _status_ok()
     assert torch.equal(ours, lib)
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 4096, 1024), (77, 2056, 528), (200, 1024, 4096), (1, 1024, 1024),
+                                   (256, 4104, 1024), (128, 16384, 2048), (64, 9216, 512)])
+@pytest.mark.parametrize("kind", ["f16", "f16_bt", "fp8", "fp8_bf16"])
+def test_panel_kernel_parity(cuda_dev, monkeypatch, M, N, K, kind):
+    """The column-panel kernel for short-and-wide problems (forced with BW_PANEL=1): panel
+    widths from 32 to 512 columns (two MMAs per k-step above 256), ragged M / N / K, both B
+    layouts of FP16, FP32 and BF16 C."""
+    import torch
+
+    monkeypatch.setenv("BW_PANEL", "1")
+    if kind.startswith("f16"):
+        A = _f16(o.seeded_uniform((M, K), 151))
+        B = _f16(o.seeded_uniform((K, N), 152))
+        bt = kind == "f16_bt"
+        C = _np(bwgemm.gemm_f16(_t(A, cuda_dev).half(), _t(B.T.copy() if bt else B, cuda_dev).half(),
+                                b_transposed=bt))
+        R = o.gemm_f64(A, B)
+        tol = o.f16_tolerance(K, np.abs(A).max(), np.abs(B).max())
+    else:
+        A = o.seeded_normal((M, K), 153)
+        B = o.seeded_normal((K, N), 154)
+        qa, sa = bwgemm.quantize_fp8(_t(A, cuda_dev), False, bwgemm.SCALE_AMAX)
+        qb, sb = bwgemm.quantize_fp8(_t(B, cuda_dev), True, bwgemm.SCALE_AMAX)
+        bf16 = kind == "fp8_bf16"
+        C = _np(bwgemm.gemm_fp8(qa, qb, sa, sb, out_dtype=bwgemm.OUT_BF16 if bf16 else bwgemm.OUT_F32))
+        ra, rsa = o.quant_fp8(A, False, o.SCALE_AMAX)
+        rb, rsb = o.quant_fp8(B, True, o.SCALE_AMAX)
+        R = o.gemm_f64(o.dequant_fp8(ra), o.dequant_fp8(rb), b_trans=True) * float(np.float32(rsa) * np.float32(rsb))
+        tol = o.lowp_tolerance(K, 448 * rsa, 448 * rsb, np.abs(R).max(), bf16)
+    torch.cuda.synchronize()
+    _status_ok()
+    assert np.abs(C - R).max() <= tol
