@@ -57,6 +57,7 @@ SHAPE = [DIM, DIM, DIM]  # M, N (per GPU), K; --shape overrides (e.g. the skinny
 SHARDED = (16384, 65536, 8192)  # M, N_total, K
 SKINNY = (128, 65536, 8192)
 NUM_SMS = 148
+_MULTICAST_BUFFERS = []  # symmetric-memory buffers bound to a multicast object (see multicast_gather)
 
 
 def load_peaks():
@@ -643,6 +644,15 @@ def run_sharded(args, world, rank, dev, stream):
                 "target_ms": round(floor_ms, 4), "frac": round(floor_ms / rec["fused_gather"]["ms_per_step"], 4),
                 "how": "max(GEMM time, bytes sent per rank / 770 GB/s measured peer-copy rate)",
                 "limiter": "NVLink egress of the gathered C" if sent / (link * 1e9) * 1e3 > ms else "GEMM"}
+            if not args.no_multicast:
+                mc = multicast_gather(wl, operands, C, full, world, rank, dev, stream, steps)
+                if mc.get("ms_per_step"):
+                    mc["tflops_all_gpus"] = round(tflops(total_flops, mc["ms_per_step"]), 2)
+                    sent_mc = int(C.numel() * C.element_size())
+                    floor_mc = max(ms, sent_mc / (link * 1e9) * 1e3)
+                    mc["roofline"] = {"target_ms": round(floor_mc, 4), "frac": round(floor_mc / mc["ms_per_step"], 4),
+                                      "how": "max(GEMM time, shard bytes leaving each GPU once / 770 GB/s)"}
+                rec["fused_gather_multicast"] = mc
             del full
         out[wl] = rec
         del C
@@ -695,6 +705,45 @@ def fused_gather(args, wl, operands, C, full, world, rank, dev, stream, steps):
     return {"ms_per_step": round(ms, 4), "bytes_sent_per_rank": int(C.numel() * C.element_size() * (world - 1)),
             "matches_nccl_gather_on_all_ranks": same_all,
             "how": "one kernel: each staged 32-row chunk is TMA-stored to the local C and to every peer's C over NVLink"}
+
+
+def multicast_gather(wl, operands, C, full, world, rank, dev, stream, steps):
+    """GEMM and all-gather in one kernel through NVSwitch multicast: every rank binds its C_full
+    to one NVLink multicast object (torch symmetric memory) and the epilogue writes each staged
+    chunk once with multimem.st, which the switch replicates into every rank's C_full. Timed
+    like the GEMM; checked bit-for-bit against the NCCL gather on every rank."""
+    import torch
+
+    import bwgemm
+    import sharding
+
+    M, N = C.shape
+    try:
+        mcC = sharding.MulticastC(M, N * world, C.dtype, dev)
+    except Exception as ex:  # no symmetric-memory multicast on this platform
+        return {"unavailable": f"{type(ex).__name__}: {ex}"[:200]}
+    # kept until the process ends: no rank unbinds its memory from the multicast object while
+    # another rank may still use it
+    _MULTICAST_BUFFERS.append(mcC)
+    if not mcC.available:
+        return {"unavailable": "symmetric memory reports no multicast address (no NVLS on this platform)"}
+    if wl == "f16":
+        A, B = operands
+        step = lambda: bwgemm.gemm_f16_allgather_multicast(A, B, mcC.mc, world, rank, N * world, stream=stream)  # noqa: E731
+    else:
+        qa, qb, sa, sb = operands
+        step = lambda: bwgemm.gemm_fp8_allgather_multicast(qa, qb, sa, sb, mcC.mc, world, rank, N * world,  # noqa: E731
+                                                           stream=stream)
+    ms = timed_steps(step, steps, 3, world, stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    same = bool(torch.equal(mcC.C, full))
+    same_all = max_over_ranks(0.0 if same else 1.0, world) == 0.0
+    barrier(world)
+    return {"ms_per_step": round(ms, 4), "bytes_leaving_each_gpu": int(C.numel() * C.element_size()),
+            "matches_nccl_gather_on_all_ranks": same_all,
+            "how": "one kernel: each staged 32-row chunk is written once with multimem.st to the multicast "
+                   "address; NVSwitch replicates it into every rank's C"}
 
 
 def run_sustained(step, flops, ms_hint, stream, clocks, peaks, peak_src, seconds=2.5):
@@ -930,6 +979,7 @@ def main():
     ap.add_argument("--shape", default=None, help="MxNxK per GPU (default 8192x8192x8192, BASELINE configs[1])")
     ap.add_argument("--no-extra", action="store_true", help="headline, e2e and comparisons only")
     ap.add_argument("--no-compare", action="store_true")
+    ap.add_argument("--no-multicast", action="store_true", help="skip the NVSwitch multicast fused gather")
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()
     if args.shape:

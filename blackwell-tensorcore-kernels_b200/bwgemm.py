@@ -94,6 +94,8 @@ def lib():
         "bw_gemm_sharded": [I, I, P, I, I, I, I, I],
         "bw_gemm_f16_allgather": [P, P, P, P, I, I, I, I, I, P],
         "bw_gemm_fp8_allgather": [P, P, P, P, P, I, P, I, I, I, I, I, P],
+        "bw_gemm_f16_allgather_multicast": [P, P, P, I, I, I, I, I, P],
+        "bw_gemm_fp8_allgather_multicast": [P, P, P, P, P, I, I, I, I, I, I, P],
         "bw_ipc_malloc": [ctypes.c_size_t, P, P],
         "bw_ipc_free": [P],
         "bw_ipc_open": [P, P],
@@ -383,3 +385,19 @@ def gemm_fp8_allgather(A, Bt_shard, scale_a, scale_b, C_full, peers, rank: int, 
     _check(lib().bw_gemm_fp8_allgather(_ptr(A), _ptr(Bt_shard), _ptr(scale_a), _ptr(scale_b), _ptr(C_full),
                                        out_dtype, _peer_array(peers), world, rank, M, C_full.shape[1], K,
                                        _stream(stream)))
+
+
+def gemm_f16_allgather_multicast(A, B_shard, mc_ptr: int, world: int, rank: int, N_total: int, stream=None):
+    """This rank's columns of the M x N_total product, written once through the multicast
+    address `mc_ptr` (every rank's buffer bound to one NVLink multicast object) and so into
+    every rank's C."""
+    M, K = A.shape
+    _check(lib().bw_gemm_f16_allgather_multicast(_ptr(A), _ptr(B_shard), mc_ptr, world, rank, M, N_total, K,
+                                                 _stream(stream)))
+
+
+def gemm_fp8_allgather_multicast(A, Bt_shard, scale_a, scale_b, mc_ptr: int, world: int, rank: int, N_total: int,
+                                 out_dtype=OUT_BF16, stream=None):
+    M, K = A.shape
+    _check(lib().bw_gemm_fp8_allgather_multicast(_ptr(A), _ptr(Bt_shard), _ptr(scale_a), _ptr(scale_b), mc_ptr,
+                                                 out_dtype, world, rank, M, N_total, K, _stream(stream)))

@@ -181,6 +181,8 @@ struct GatherCtx {
   int col0;
   int npeers;
   void* peers[7];
+  void* mc = nullptr;  // multicast address of C_full (all ranks bound): replaces the peer stores
+  int mc_plain = 0;
 };
 
 GemmParams base_params(const DeviceState& d, void* C, int M, int N, int K) {
@@ -364,6 +366,11 @@ void gather_apply(const GatherCtx* g, GemmParams& p, int elem) {
   p.ldc = g->ldc;
   p.npeers = g->npeers;
   for (int i = 0; i < g->npeers; ++i) p.peers[i] = static_cast<char*>(g->peers[i]) + static_cast<size_t>(g->col0) * elem;
+  if (g->mc) {
+    p.mc = static_cast<char*>(g->mc) + static_cast<size_t>(g->col0) * elem;
+    p.mc_plain = g->mc_plain;
+    p.C = nullptr;  // only multimem stores may touch a multicast address
+  }
 }
 
 int gemm_f16_impl(const void* A, const void* B, float* C, int M, int N, int K, cudaStream_t s, bool b_mn,
@@ -404,7 +411,11 @@ int gemm_f16_impl(const void* A, const void* B, float* C, int M, int N, int K, c
   if (g) {
     PeerMaps pm{};
     CUtensorMap tcl;
-    if ((r = make_c_map_ld(&tcl, p.C, M, N, g->ldc, BW_OUT_F32)) != BW_OK) return r;
+    // With a multicast C the epilogue writes through multimem.st and no TMA store runs: the
+    // C tensor map is a placeholder over A (local memory, never copied to or from).
+    if (g->mc) r = make_c_map_ld(&tcl, const_cast<void*>(A), 8, 8, 8, BW_OUT_F32);
+    else r = make_c_map_ld(&tcl, p.C, M, N, g->ldc, BW_OUT_F32);
+    if (r != BW_OK) return r;
     for (int q = 0; q < p.npeers; ++q)
       if ((r = make_c_map_ld(&pm.m[q], p.peers[q], M, N, g->ldc, BW_OUT_F32)) != BW_OK) return r;
     return launch_pair<Kind::F16, true, 3, Out::F32, false, 2>(ta, tb, tcl, p, s, *d, &pm);
@@ -473,7 +484,9 @@ int gemm_fp8_impl(const uint8_t* A, const uint8_t* Bt, const float* sa, const fl
   if (g) {
     PeerMaps pm{};
     CUtensorMap tcl;
-    if ((r = make_c_map_ld(&tcl, p.C, M, N, g->ldc, out_dtype)) != BW_OK) return r;
+    if (g->mc) r = make_c_map_ld(&tcl, const_cast<uint8_t*>(A), 8, 8, 8, out_dtype);  // placeholder (see f16)
+    else r = make_c_map_ld(&tcl, p.C, M, N, g->ldc, out_dtype);
+    if (r != BW_OK) return r;
     for (int q = 0; q < p.npeers; ++q)
       if ((r = make_c_map_ld(&pm.m[q], p.peers[q], M, N, g->ldc, out_dtype)) != BW_OK) return r;
     if (out_dtype == BW_OUT_F32) return launch_pair<Kind::F8, false, 3, Out::F32, false, 2>(ta, tb, tcl, p, s, *d, &pm);
@@ -616,6 +629,38 @@ int bw_gemm_fp8_allgather(const uint8_t* A, const uint8_t* Bt_shard, const float
   int r = make_gather(&g, peer_C_full, world, rank, N_total);
   if (r != BW_OK) return r;
   return gemm_fp8_impl(A, Bt_shard, scale_a, scale_b, C_full, out_dtype, M, N_total / world, K,
+                       static_cast<cudaStream_t>(stream), &g);
+}
+
+static int make_gather_mc(GatherCtx* g, void* C_multicast, int world, int rank, int N_total) {
+  if (world < 1 || world > 8 || rank < 0 || rank >= world)
+    return set_error(BW_ERR_INVALID, "multicast gather: rank %d of world %d (1..8 ranks)", rank, world);
+  if (N_total % world != 0) return set_error(BW_ERR_INVALID, "N_total=%d not divisible by world=%d", N_total, world);
+  if (!C_multicast) return set_error(BW_ERR_INVALID, "multicast gather: C_multicast is null");
+  g->ldc = N_total;
+  g->col0 = rank * (N_total / world);
+  g->npeers = 0;
+  g->mc = C_multicast;
+  g->mc_plain = env_int("BW_MC_PLAIN", 0) != 0 ? 1 : 0;
+  return BW_OK;
+}
+
+int bw_gemm_f16_allgather_multicast(const void* A, const void* B_shard, void* C_multicast, int world, int rank,
+                                    int M, int N_total, int K, void* stream) {
+  GatherCtx g;
+  int r = make_gather_mc(&g, C_multicast, world, rank, N_total);
+  if (r != BW_OK) return r;
+  return gemm_f16_impl(A, B_shard, static_cast<float*>(C_multicast), M, N_total / world, K,
+                       static_cast<cudaStream_t>(stream), true, &g);
+}
+
+int bw_gemm_fp8_allgather_multicast(const uint8_t* A, const uint8_t* Bt_shard, const float* scale_a,
+                                    const float* scale_b, void* C_multicast, int out_dtype, int world, int rank,
+                                    int M, int N_total, int K, void* stream) {
+  GatherCtx g;
+  int r = make_gather_mc(&g, C_multicast, world, rank, N_total);
+  if (r != BW_OK) return r;
+  return gemm_fp8_impl(A, Bt_shard, scale_a, scale_b, C_multicast, out_dtype, M, N_total / world, K,
                        static_cast<cudaStream_t>(stream), &g);
 }
 

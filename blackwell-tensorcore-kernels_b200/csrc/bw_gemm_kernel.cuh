@@ -85,6 +85,12 @@ struct GemmParams {
   // CUDA IPC) at this shard's column offset; each staged chunk is also TMA-stored there.
   void* peers[7];
   int npeers;
+  // Fused all-gather through NVSwitch multicast (staged epilogue): `mc` is the multicast
+  // address of the M x ldc C that every rank has bound, at this shard's column offset; each
+  // staged chunk is written once with multimem.st and lands in every rank's C. mc_plain = 1
+  // writes it with plain stores instead (a single-GPU check of the same indexing).
+  void* mc;
+  int mc_plain;
 };
 
 template <Kind KIND, bool B_MN, int BN, int STAGES, int ACC_BUFS>
@@ -190,7 +196,8 @@ template <Out OUT, int NCOLS, typename Release>
 __device__ __forceinline__ void epilogue_tile(uint32_t tbase, const CUtensorMap* tmC, int x0, int y0, float alpha,
                                               uint8_t* wbuf, int& uses, int lane, uint64_t store_policy,
                                               bool hinted, Release release, bool reduce_add = false,
-                                              const PeerMaps* peer_maps = nullptr, int npeers = 0) {
+                                              const PeerMaps* peer_maps = nullptr, int npeers = 0,
+                                              const GemmParams* mcp = nullptr) {
   constexpr int kCols = (OUT == Out::F32) ? 32 : 64;  // columns per 128-byte row chunk
   static_assert(NCOLS % kCols == 0, "tile width must be whole 128-byte chunks");
   const uint32_t row_addr = smem_u32(wbuf) + lane * 128;
@@ -228,6 +235,28 @@ __device__ __forceinline__ void epilogue_tile(uint32_t tbase, const CUtensorMap*
     }
     fence_proxy_async_smem();
     __syncwarp();
+    if (mcp != nullptr) {
+      // Multicast gather: the warp copies the staged 32 x 128 B chunk out in 16-byte pieces,
+      // 8 lanes per row (whole 128-byte lines), clipped to C like the TMA store would be.
+      constexpr int kElemsPer16 = (OUT == Out::F32) ? 4 : 8;
+      constexpr int kElemBytes = (OUT == Out::F32) ? 4 : 2;
+      const uint32_t sbase = smem_u32(wbuf) + bsel * kEpiBufBytes;
+#pragma unroll
+      for (int it = 0; it < 8; ++it) {
+        const int li = it * 32 + lane;
+        const int i = li >> 3, j = li & 7;
+        const int row = y0 + i, col = x0 + c + j * kElemsPer16;
+        if (row < mcp->M && col < mcp->N) {
+          const uint4 v = ld_shared_v4(sbase + i * 128 + ((j ^ (i & 7)) << 4));
+          char* dst = static_cast<char*>(mcp->mc) + (static_cast<size_t>(row) * mcp->ldc + col) * kElemBytes;
+          if (mcp->mc_plain) st_global_v4(dst, v);
+          else multimem_st_v4(dst, v);
+        }
+      }
+      __syncwarp();
+      ++uses;
+      continue;
+    }
     if (lane == 0) {
       if (reduce_add) tma_reduce_add_2d(tmC, wbuf + bsel * kEpiBufBytes, x0 + c, y0);
       else if (hinted) tma_store_2d_hint(tmC, wbuf + bsel * kEpiBufBytes, x0 + c, y0, store_policy);

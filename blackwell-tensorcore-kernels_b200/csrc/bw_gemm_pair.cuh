@@ -219,10 +219,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const int row0 = tm * TM + static_cast<int>(rank) * 128 + q * 32;
       if constexpr (DIRECT_EPI) epilogue_tile_direct<OUT, TN>(tbase, p, row0 + lane, tn * TN, alpha, release);
       else epilogue_tile<OUT, TN>(tbase, &tmC, tn * TN, row0, alpha, wbuf, uses, lane, store_pol,
-                                  (p.hints & 2) != 0, release, false, &pm, p.npeers);
+                                  (p.hints & 2) != 0, release, false, &pm, p.npeers, p.mc ? &p : nullptr);
       if (tracing) { tr_b += clock64() - w4; ++tr_c; }
     }
     if (lane == 0) bulk_wait_group<0>();
+    if (p.mc) __threadfence_system();  // multicast stores performed before the grid completes
   }
 
   if (tracing && lane == 0) {

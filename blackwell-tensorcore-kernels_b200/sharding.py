@@ -77,3 +77,20 @@ class SymmetricC:
                 bwgemm.ipc_close(p)
         self.peers = []
         self.buf.close()
+
+
+class MulticastC:
+    """Row-major M x N_total C in torch symmetric memory, bound on every rank to one NVLink
+    multicast object: the target of the multicast fused GEMM + all-gather
+    (bwgemm.gemm_*_allgather_multicast), whose multimem stores NVSwitch replicates into every
+    rank's copy. Collective (every rank constructs it with the same shape). `available` is
+    False where the platform offers no multicast (then `mc` is 0 and nothing may use it)."""
+
+    def __init__(self, M: int, N_total: int, dtype, device, group=None):
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+
+        self.C = symm_mem.empty((M, N_total), dtype=dtype, device=device)
+        self.handle = symm_mem.rendezvous(self.C, group if group is not None else dist.group.WORLD)
+        self.mc = int(getattr(self.handle, "multicast_ptr", 0) or 0)
+        self.available = self.mc != 0

@@ -177,6 +177,20 @@ int bw_gemm_fp8_allgather(const uint8_t* A, const uint8_t* Bt_shard, const float
                           void* C_full, int out_dtype, void* const* peer_C_full, int world, int rank, int M,
                           int N_total, int K, void* stream);
 
+/* Fused all-gather through NVSwitch multicast (one process per GPU, 1..8 ranks). C_multicast is
+ * the multicast address of a row-major M x N_total buffer that every rank has bound to one
+ * NVLink multicast object (e.g. torch symmetric memory's multicast_ptr); rank r computes columns
+ * [r*N_total/world, (r+1)*N_total/world) and its epilogue writes each staged 32-row chunk once
+ * with multimem.st, which NVSwitch replicates into every rank's buffer: one copy of the shard
+ * leaves each GPU instead of world - 1. Completion as for bw_gemm_f16_allgather (synchronise,
+ * then barrier across ranks). BW_MC_PLAIN=1 writes with plain stores instead, for checking the
+ * indexing on one GPU with an ordinary buffer. No counterpart in the reference (single GPU). */
+int bw_gemm_f16_allgather_multicast(const void* A, const void* B_shard, void* C_multicast, int world, int rank,
+                                    int M, int N_total, int K, void* stream);
+int bw_gemm_fp8_allgather_multicast(const uint8_t* A, const uint8_t* Bt_shard, const float* scale_a,
+                                    const float* scale_b, void* C_multicast, int out_dtype, int world, int rank,
+                                    int M, int N_total, int K, void* stream);
+
 /* Device buffers shareable across processes (CUDA IPC, 64-byte handles): bw_ipc_malloc returns
  * the buffer (256-byte aligned) and its handle; another process maps it with bw_ipc_open. */
 enum { BW_IPC_HANDLE_BYTES = 64 };
