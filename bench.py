@@ -644,7 +644,7 @@ def run_sharded(args, world, rank, dev, stream):
                 "target_ms": round(floor_ms, 4), "frac": round(floor_ms / rec["fused_gather"]["ms_per_step"], 4),
                 "how": "max(GEMM time, bytes sent per rank / 770 GB/s measured peer-copy rate)",
                 "limiter": "NVLink egress of the gathered C" if sent / (link * 1e9) * 1e3 > ms else "GEMM"}
-            if not args.no_multicast:
+            if args.multicast:
                 mc = multicast_gather(wl, operands, C, full, world, rank, dev, stream, steps)
                 if mc.get("ms_per_step"):
                     mc["tflops_all_gpus"] = round(tflops(total_flops, mc["ms_per_step"]), 2)
@@ -979,7 +979,8 @@ def main():
     ap.add_argument("--shape", default=None, help="MxNxK per GPU (default 8192x8192x8192, BASELINE configs[1])")
     ap.add_argument("--no-extra", action="store_true", help="headline, e2e and comparisons only")
     ap.add_argument("--no-compare", action="store_true")
-    ap.add_argument("--no-multicast", action="store_true", help="skip the NVSwitch multicast fused gather")
+    ap.add_argument("--multicast", action="store_true",
+                    help="also time the fused gather through NVSwitch multicast (multimem.st)")
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()
     if args.shape:
