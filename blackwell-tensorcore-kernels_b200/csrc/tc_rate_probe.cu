@@ -10,7 +10,8 @@
 // achieved TFLOP/s and, combined with the cycle count, the effective SM clock.
 //
 // Variants: f16 (kind::f16, M128 N256 K16), e4m3 (kind::f8f6f4, K32), mxf4 (kind::mxf4
-// block32, packed E2M1 with 2^0 scales, K64), f16x2 (cta_group::2, M256 N256 K16 per pair).
+// block32, packed E2M1 with 2^0 scales, K64), f16x2 (cta_group::2, M256 N256 K16 per pair),
+// mxf4 pairs (cta_group::2, M256 with N 256 / 128 / 192 / 224, K64).
 //   tc_rate_probe [iters=4096] [reps=5] [csv_out]
 #include <cuda_runtime.h>
 
@@ -30,7 +31,8 @@ constexpr int kABytes = 128 * 128;   // 128 rows x 128 B
 constexpr int kBBytes = 256 * 128;   // 256 rows x 128 B
 constexpr int kSfBytes = 2 * 512;    // scale factors for mxf4: A + B atoms
 
-template <int VARIANT>  // 0 f16, 1 e4m3, 2 mxf4, 3 f16 cta pair
+// 0 f16, 1 e4m3, 2 mxf4, 3 f16 cta pair, mxf4 pairs: 4 N256, 5 N128, 6 N192, 7 N224
+template <int VARIANT>
 __global__ void __launch_bounds__(kThreads, 1) k_rate(int iters, unsigned long long* cycles, int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -41,12 +43,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_rate(int iters, unsigned long l
   uint32_t* slot = reinterpret_cast<uint32_t*>(bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(slot + 1);
   const int warp = threadIdx.x >> 5;
-  constexpr bool kPair = VARIANT == 3;
+  constexpr bool kPair = VARIANT >= 3;
+  constexpr bool kMx = VARIANT == 2 || VARIANT >= 4;
 
   // Operand pattern: small values (0x3c/0x38 patterns are ~1.0 in f16/e4m3; nibbles 0x2 =
   // 1.0 in e2m1) so no lane produces Inf/NaN. Scale factors 0x7f = 2^0.
   for (int i = threadIdx.x; i < (kABytes + kBBytes) / 4; i += kThreads)
-    reinterpret_cast<uint32_t*>(smem)[i] = (VARIANT == 2) ? 0x22222222u : (VARIANT == 1 ? 0x38303830u : 0x3c003800u);
+    reinterpret_cast<uint32_t*>(smem)[i] = kMx ? 0x22222222u : (VARIANT == 1 ? 0x38303830u : 0x3c003800u);
   for (int i = threadIdx.x; i < kSfBytes / 4; i += kThreads) reinterpret_cast<uint32_t*>(sSF)[i] = 0x7f7f7f7fu;
   fence_proxy_async_smem();
   if (threadIdx.x == 0) {
@@ -70,8 +73,17 @@ __global__ void __launch_bounds__(kThreads, 1) k_rate(int iters, unsigned long l
       tmem_cp_32x128b_warpx4(tmem + 256, sdesc_noswz(sf, 16, 128));
       tmem_cp_32x128b_warpx4(tmem + 260, sdesc_noswz(sf + 512, 16, 128));
     }
-    const uint32_t idesc = VARIANT == 2 ? idesc_mxf4(128, 256, 0, 0)
-                         : idesc_dense(0, 0, false, kPair ? 256 : 128, 256);
+    if constexpr (VARIANT >= 4) {  // SFA at column 256, SFB (two 128-row blocks) at 260 and 264
+      tmem_cp_32x128b_warpx4_pair(tmem + 256, sdesc_noswz(sf, 16, 128));
+      tmem_cp_32x128b_warpx4_pair(tmem + 260, sdesc_noswz(sf + 512, 16, 128));
+      tmem_cp_32x128b_warpx4_pair(tmem + 264, sdesc_noswz(sf + 512, 16, 128));
+    }
+    const uint32_t idesc = VARIANT == 2   ? idesc_mxf4(128, 256, 0, 0)
+                         : VARIANT == 4 ? idesc_mxf4(256, 256, 0, 0)
+                         : VARIANT == 5 ? idesc_mxf4(256, 128, 0, 0)
+                         : VARIANT == 6 ? idesc_mxf4(256, 192, 0, 0)
+                         : VARIANT == 7 ? idesc_mxf4(256, 224, 0, 0)
+                                        : idesc_dense(0, 0, false, kPair ? 256 : 128, 256);
     const long long t0 = clock64();
 #pragma unroll 1
     for (int it = 0; it < iters; ++it) {
@@ -83,6 +95,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_rate(int iters, unsigned long l
         if constexpr (VARIANT == 0) umma_f16(tmem, ad, bd, idesc, acc);
         else if constexpr (VARIANT == 1) umma_f8f6f4(tmem, ad, bd, idesc, acc);
         else if constexpr (VARIANT == 2) umma_mxf4(tmem, ad, bd, idesc, tmem + 256, tmem + 260, acc);
+        else if constexpr (VARIANT >= 4) umma_mxf4_pair(tmem, ad, bd, idesc, tmem + 256, tmem + 260, acc);
         else umma_f16_pair(tmem, ad, bd, idesc, acc);
       }
     }
@@ -129,8 +142,17 @@ int main(int argc, char** argv) {
   CK(cudaFuncSetAttribute(k_rate<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   CK(cudaFuncSetAttribute(k_rate<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   CK(cudaFuncSetAttribute(k_rate<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  const char* names[4] = {"f16_m128n256k16", "e4m3_m128n256k32", "mxf4_m128n256k64", "f16_pair_m256n256k16"};
-  const double kflop[4] = {2.0 * 128 * 256 * 16, 2.0 * 128 * 256 * 32, 2.0 * 128 * 256 * 64, 2.0 * 256 * 256 * 16};
+  CK(cudaFuncSetAttribute(k_rate<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  CK(cudaFuncSetAttribute(k_rate<5>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  CK(cudaFuncSetAttribute(k_rate<6>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  CK(cudaFuncSetAttribute(k_rate<7>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  constexpr int kVariants = 8;
+  const char* names[kVariants] = {"f16_m128n256k16",       "e4m3_m128n256k32",      "mxf4_m128n256k64",
+                                  "f16_pair_m256n256k16",  "mxf4_pair_m256n256k64", "mxf4_pair_m256n128k64",
+                                  "mxf4_pair_m256n192k64", "mxf4_pair_m256n224k64"};
+  const double kflop[kVariants] = {2.0 * 128 * 256 * 16, 2.0 * 128 * 256 * 32, 2.0 * 128 * 256 * 64,
+                                   2.0 * 256 * 256 * 16, 2.0 * 256 * 256 * 64, 2.0 * 256 * 128 * 64,
+                                   2.0 * 256 * 192 * 64, 2.0 * 256 * 224 * 64};
   FILE* f = csv ? fopen(csv, "w") : nullptr;
   if (f) fprintf(f, "variant,rep,ms,tflops,flop_per_sm_clk,sm_mhz_effective\n");
   printf("%-22s %4s %9s %9s %14s %10s\n", "variant", "rep", "ms", "TFLOP/s", "FLOP/SM/clk", "SM MHz");
@@ -139,10 +161,11 @@ int main(int argc, char** argv) {
   CK(cudaEventCreate(&e1));
   std::vector<unsigned long long> cyc(sms);
   for (int rep = 0; rep < reps; ++rep) {
-    for (int v = 0; v < 4; ++v) {
-      const int grid = (v == 3) ? (sms / 2) * 2 : sms;
+    for (int v = 0; v < kVariants; ++v) {
+      const bool pair = v >= 3;
+      const int grid = pair ? (sms / 2) * 2 : sms;
       auto launch = [&] {
-        if (v == 3) {
+        if (pair) {
           cudaLaunchConfig_t cfg = {};
           cfg.gridDim = dim3(grid);
           cfg.blockDim = dim3(kThreads);
@@ -154,7 +177,11 @@ int main(int argc, char** argv) {
           at.val.clusterDim.z = 1;
           cfg.attrs = &at;
           cfg.numAttrs = 1;
-          CK(cudaLaunchKernelEx(&cfg, k_rate<3>, iters, dcyc, dstat));
+          if (v == 3) CK(cudaLaunchKernelEx(&cfg, k_rate<3>, iters, dcyc, dstat));
+          else if (v == 4) CK(cudaLaunchKernelEx(&cfg, k_rate<4>, iters, dcyc, dstat));
+          else if (v == 5) CK(cudaLaunchKernelEx(&cfg, k_rate<5>, iters, dcyc, dstat));
+          else if (v == 6) CK(cudaLaunchKernelEx(&cfg, k_rate<6>, iters, dcyc, dstat));
+          else CK(cudaLaunchKernelEx(&cfg, k_rate<7>, iters, dcyc, dstat));
         } else if (v == 0) {
           k_rate<0><<<grid, kThreads, smem>>>(iters, dcyc, dstat);
         } else if (v == 1) {
@@ -178,10 +205,10 @@ int main(int argc, char** argv) {
         if (cyc[i]) per.push_back(cyc[i]);
       std::sort(per.begin(), per.end());
       const double med = per.empty() ? 0 : per[per.size() / 2];
-      const int issuers = v == 3 ? grid / 2 : grid;
+      const int issuers = pair ? grid / 2 : grid;
       const double flop_instr = kflop[v] * 4.0 * iters;
       // per SM: a pair instruction's work is split over two SMs
-      const double per_sm_clk = med > 0 ? flop_instr / med / (v == 3 ? 2.0 : 1.0) : 0;
+      const double per_sm_clk = med > 0 ? flop_instr / med / (pair ? 2.0 : 1.0) : 0;
       const double tflops = flop_instr * issuers / (ms * 1e-3) / 1e12;
       const double mhz = med > 0 ? med / (ms * 1e3) : 0;
       printf("%-22s %4d %9.3f %9.1f %14.1f %10.0f\n", names[v], rep, ms, tflops, per_sm_clk, mhz);
