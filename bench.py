@@ -70,13 +70,13 @@ def load_peaks():
         return dict(FALLBACK_PEAKS), "fallback"
 
 
-def profile_traffic(name: str):
+def profile_traffic(name: str, key: str = "traffic_bytes_per_launch"):
     """DRAM bytes per launch recorded from an ncu capture in profiles/<name>.md
-    (line `traffic_bytes_per_launch: <int>`), or None."""
+    (line `<key>: <int>`), or None."""
     path = os.path.join(REPO, "profiles", name + ".md")
     try:
         for line in open(path):
-            if line.strip().startswith("traffic_bytes_per_launch:"):
+            if line.strip().startswith(key + ":"):
                 return int(float(line.split(":", 1)[1]))
     except OSError:
         pass
@@ -553,21 +553,22 @@ def run_precisions(args, dev, stream, peaks, peak_src):
     del fin
     n_in = {"f16": Ms * Ks * 2 + Ks * Ns * 2 + Ms * Ns * 4, "fp8": Ms * Ks + Ks * Ns + Ms * Ns * 2}
 
-    def skinny_record(name, ours, lib, lib_name, nbytes, err, tol, kind):
+    def skinny_record(name, ours, lib, lib_name, nbytes, err, tol, kind, traffic):
         ms = timed_steps(ours, args.steps, args.warmup, 1, stream)
         a, b = interleaved(ours, lib, block, stream, sflops)
         gbs = nbytes / (ms * 1e-3) / 1e9
         out[name] = {"workload": f"{name.split('_')[1]}_gemm_{Ms}x{Ns}x{Ks}", "quantisation": kind,
                      "ms_per_step": round(ms, 4), "tflops": round(tflops(sflops, ms), 2),
                      "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": round(hbm, 1), "unit": "GB/s",
-                                  "frac": round(gbs / hbm, 4), "traffic": None,
+                                  "frac": round(gbs / hbm, 4), "traffic": traffic,
                                   "algorithmic_bytes_per_launch": nbytes, "peak_source": f"{peak_src}: hbm_gbs"},
                      "interleaved": {"ours_tflops": a, "library_tflops": b, "library": lib_name, "block_steps": block},
                      "max_abs_err": err, "tolerance": tol, "within_tolerance": err <= tol}
 
     skinny_record("skinny_f16", lambda: bwgemm.gemm_f16(A, B, Cf, stream=stream),
                   lambda: torch.mm(A, B, out_dtype=torch.float32), "cuBLAS (torch.mm fp16 -> fp32)", n_in["f16"],
-                  err, tol, "FP16 uniform[-1, 1], FP32 C (split-K)")
+                  err, tol, "FP16 uniform[-1, 1], FP32 C (column-panel kernel, one 128 x 448 unit per SM)",
+                  profile_traffic("bw_tc_gemm_panel_128x65536x8192", "traffic_bytes_per_launch_f16"))
     del A, B, Cf
     sin = make_inputs("fp8", 0, dev, SKINNY)
     qa, sa = bwgemm.quantize_fp8(sin["A32"], False, bwgemm.SCALE_AMAX)
@@ -585,7 +586,8 @@ def run_precisions(args, dev, stream, peaks, peak_src):
     skinny_record("skinny_fp8", lambda: bwgemm.gemm_fp8(qa, qb, sa, sb, Cb, stream=stream),
                   lambda: torch._scaled_mm(a8, b8, scale_a=sa, scale_b=sb, out_dtype=torch.bfloat16),
                   "cuBLASLt FP8 (torch._scaled_mm, BF16 out)", n_in["fp8"], err, tol,
-                  "E4M3 amax/448, BF16 C (split-K into an FP32 workspace)")
+                  "E4M3 amax/448, BF16 C (column-panel kernel, one 128 x 448 unit per SM)",
+                  profile_traffic("bw_tc_gemm_panel_128x65536x8192"))
     return out
 
 

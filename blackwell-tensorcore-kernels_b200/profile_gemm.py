@@ -1,4 +1,5 @@
-"""Small driver for profiling one GEMM kind under ncu: KIND=f16|fp8|fp4|mxfp4, N=size (square).
+"""Small driver for profiling one GEMM kind under ncu: KIND=f16|fp8|fp4|mxfp4, N=size (square),
+or M / N / K separately (M=128 N=65536 K=8192 is the skinny shape).
 Runs the GEMM three times (ncu -s 1 -c 1 then captures the second launch). KIND=quant instead
 runs three rounds of the quantisers on an N x N FP32 input: MXFP4 rows, MXFP4 columns (the Bt
 operand) and a transposed E4M3 with the fixed scale (ncu -k regex:k_quant -s 3 -c 3 captures
@@ -15,7 +16,7 @@ import torch, bwgemm
 bwgemm.init(0)
 dev = torch.device('cuda:0')
 kind = os.environ.get('KIND', 'f16'); n = int(os.environ.get('N', '8192'))
-M = N = K = n
+M = int(os.environ.get('M', n)); N = n; K = int(os.environ.get('K', n))
 if kind == 'f16':
     A = torch.randn(M, K, device=dev).half(); B = torch.randn(K, N, device=dev).half(); C = torch.empty(M, N, device=dev)
     f = lambda: bwgemm.gemm_f16(A, B, C)
