@@ -249,6 +249,7 @@ bool use_narrow(int M, int N, const DeviceState& d) {
 int panel_width(int M, int N, int K, bool gran64, const void* C, int elem, const DeviceState& d) {
   const int forced = env_int("BW_PANEL", -1);
   if (forced == 0 || M > 256 || !direct_epilogue_ok(C, N, elem)) return 0;
+  if (forced != 1 && env_int("BW_SPLITK", -1) >= 1) return 0;  // an explicit split count asks for split-K
   if (forced != 1 && K < 512) return 0;
   const int gran = gran64 ? 64 : 32;
   const long tiles_m = (M + 127) / 128;
