@@ -63,12 +63,12 @@ int pair_clusters_resident(Kernel kern, int threads, int smem_bytes, const Devic
   return n;
 }
 
-template <Kind KIND, bool B_MN, int STAGES, Out OUT, bool DIRECT_EPI, int KSUB, int TN = 256>
+template <Kind KIND, bool B_MN, int STAGES, Out OUT, bool DIRECT_EPI, int KSUB, int TN = 256, int EPI_BUFS = 2>
 int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, GemmParams p,
                 cudaStream_t stream, const DeviceState& d, const PeerMaps* pm = nullptr) {
   static const PeerMaps no_peers{};
-  using Cfg = PairCfg<KIND, STAGES, DIRECT_EPI, KSUB, TN>;
-  auto kern = bw_tc_gemm_pair_kernel<KIND, B_MN, STAGES, OUT, DIRECT_EPI, KSUB, TN>;
+  using Cfg = PairCfg<KIND, STAGES, DIRECT_EPI, KSUB, TN, EPI_BUFS>;
+  auto kern = bw_tc_gemm_pair_kernel<KIND, B_MN, STAGES, OUT, DIRECT_EPI, KSUB, TN, EPI_BUFS>;
   static bool attr_done[64] = {};
   int dev = 0;
   BW_CUDA(cudaGetDevice(&dev));
@@ -361,6 +361,15 @@ int gather_check(const GatherCtx* g, const void* C, int N, int K, int elem) {
   return BW_OK;
 }
 
+// Fused gather with remote stores: 2 pipeline stages and 6 staging buffers per epilogue warp
+// (24 KB of chunks in flight per warp instead of 8 KB) when BW_GATHER_STAGING=6, the default
+// being decided by measurement; the multicast form keeps 3 stages (its stores do not hold
+// the staging buffers).
+bool gather_deep_staging(const GatherCtx* g) {
+  if (!g || g->mc || g->npeers == 0) return false;
+  return env_int("BW_GATHER_STAGING", 2) == 6;
+}
+
 void gather_apply(const GatherCtx* g, GemmParams& p, int elem) {
   if (!g) return;
   p.C = static_cast<char*>(p.C) + static_cast<size_t>(g->col0) * elem;
@@ -419,6 +428,8 @@ int gemm_f16_impl(const void* A, const void* B, float* C, int M, int N, int K, c
     if (r != BW_OK) return r;
     for (int q = 0; q < p.npeers; ++q)
       if ((r = make_c_map_ld(&pm.m[q], p.peers[q], M, N, g->ldc, BW_OUT_F32)) != BW_OK) return r;
+    if (gather_deep_staging(g))
+      return launch_pair<Kind::F16, true, 2, Out::F32, false, 2, 256, 6>(ta, tb, tcl, p, s, *d, &pm);
     return launch_pair<Kind::F16, true, 3, Out::F32, false, 2>(ta, tb, tcl, p, s, *d, &pm);
   }
   if (pair) {
@@ -490,6 +501,11 @@ int gemm_fp8_impl(const uint8_t* A, const uint8_t* Bt, const float* sa, const fl
     if (r != BW_OK) return r;
     for (int q = 0; q < p.npeers; ++q)
       if ((r = make_c_map_ld(&pm.m[q], p.peers[q], M, N, g->ldc, out_dtype)) != BW_OK) return r;
+    if (gather_deep_staging(g)) {
+      if (out_dtype == BW_OUT_F32)
+        return launch_pair<Kind::F8, false, 2, Out::F32, false, 2, 256, 6>(ta, tb, tcl, p, s, *d, &pm);
+      return launch_pair<Kind::F8, false, 2, Out::BF16, false, 2, 256, 6>(ta, tb, tcl, p, s, *d, &pm);
+    }
     if (out_dtype == BW_OUT_F32) return launch_pair<Kind::F8, false, 3, Out::F32, false, 2>(ta, tb, tcl, p, s, *d, &pm);
     return launch_pair<Kind::F8, false, 3, Out::BF16, false, 2>(ta, tb, tcl, p, s, *d, &pm);
   }
@@ -610,8 +626,13 @@ static int make_gather(GatherCtx* g, void* const* peer_C_full, int world, int ra
   g->ldc = N_total;
   g->col0 = rank * (N_total / world);
   g->npeers = 0;
-  for (int q = 0; q < world; ++q)
+  // Each staged chunk goes to the peers in this order. Rotated by rank (rank + 1, rank + 2, ...)
+  // unless BW_PEER_ORDER=0 (0, 1, ..., every rank starting with the same peer).
+  const bool rotate = env_int("BW_PEER_ORDER", 1) != 0;
+  for (int i = 1; i <= world; ++i) {
+    const int q = rotate ? (rank + i) % world : i - 1;
     if (q != rank) g->peers[g->npeers++] = peer_C_full[q];
+  }
   return BW_OK;
 }
 

@@ -192,7 +192,10 @@ struct PeerMaps {
   CUtensorMap m[7];
 };
 
-template <Out OUT, int NCOLS, typename Release>
+// NB staging buffers per warp (a chunk's TMA stores must have read its buffer before the warp
+// reuses it): more buffers keep more store bytes in flight, which is what a fused all-gather's
+// remote stores need to cover the NVLink round trip.
+template <Out OUT, int NCOLS, typename Release, int NB = 2>
 __device__ __forceinline__ void epilogue_tile(uint32_t tbase, const CUtensorMap* tmC, int x0, int y0, float alpha,
                                               uint8_t* wbuf, int& uses, int lane, uint64_t store_policy,
                                               bool hinted, Release release, bool reduce_add = false,
@@ -208,9 +211,9 @@ __device__ __forceinline__ void epilogue_tile(uint32_t tbase, const CUtensorMap*
     if constexpr (kCols == 64) tmem_ld_32x32b_x32(tbase + c + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
     tmem_ld_wait();
     if (c + kCols >= NCOLS) release();
-    const int bsel = uses & 1;
-    if (uses >= 2) {
-      if (lane == 0) bulk_wait_group_read<1>();
+    const int bsel = uses % NB;
+    if (uses >= NB) {
+      if (lane == 0) bulk_wait_group_read<NB - 1>();
       __syncwarp();
     }
     const uint32_t base = row_addr + bsel * kEpiBufBytes;

@@ -20,7 +20,7 @@
 
 namespace bw {
 
-template <Kind KIND, int STAGES, bool DIRECT_EPI = false, int KSUB = 1, int TN = 256>
+template <Kind KIND, int STAGES, bool DIRECT_EPI = false, int KSUB = 1, int TN = 256, int EPI_BUFS = 2>
 struct PairCfg {
   static constexpr int kAtomBytes = 128 * kSlabBytes;  // 128 rows x one 128-byte swizzle atom of K
   static constexpr int kBAtomBytes = (TN / 2) * kSlabBytes;
@@ -29,7 +29,8 @@ struct PairCfg {
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kEpiOffset = STAGES * kStageBytes;
   // plain FP4 (kind::mxf4 with every block scale 2^0): 3 constant scale-factor atoms
-  static constexpr int kSfOffset = kEpiOffset + (DIRECT_EPI ? 0 : kEpiBytes);
+  static constexpr int kEpiBufs = EPI_BUFS;  // staging buffers per epilogue warp (staged epilogue)
+  static constexpr int kSfOffset = kEpiOffset + (DIRECT_EPI ? 0 : kEpiWarps * EPI_BUFS * kEpiBufBytes);
   static constexpr int kSfBytes = (KIND == Kind::MXF4) ? 3 * 512 : 0;
   static constexpr int kBarOffset = kSfOffset + kSfBytes;
   static_assert(TN % 32 == 0 && TN <= 256 && (KIND == Kind::MXF4 ? 2 * TN + 12 <= 512 : TN == 256), "tile N");
@@ -39,12 +40,12 @@ struct PairCfg {
   static constexpr int kTmemCols = 512;  // two 256-column FP32 accumulators
 };
 
-template <Kind KIND, bool B_MN, int STAGES, Out OUT, bool DIRECT_EPI, int KSUB, int TN = 256>
+template <Kind KIND, bool B_MN, int STAGES, Out OUT, bool DIRECT_EPI, int KSUB, int TN = 256, int EPI_BUFS = 2>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     bw_tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                            const __grid_constant__ CUtensorMap tmC, const __grid_constant__ PeerMaps pm,
                            const GemmParams p) {
-  using Cfg = PairCfg<KIND, STAGES, DIRECT_EPI, KSUB, TN>;
+  using Cfg = PairCfg<KIND, STAGES, DIRECT_EPI, KSUB, TN, EPI_BUFS>;
   static_assert(!B_MN || TN == 256, "N-major B is loaded as 64-column boxes of a 256-wide tile");
   constexpr int KX = KindTraits<KIND>::kCoordPerSlab;          // tensor-map units per swizzle atom
   constexpr int KE = KindTraits<KIND>::kElemsPerSlab * KSUB;   // K elements per pipeline stage
@@ -193,7 +194,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
     const int q = warp & 3;
     const uint64_t store_pol = l2_policy_evict_first();
-    uint8_t* wbuf = smem + Cfg::kEpiOffset + (warp - 2) * 2 * kEpiBufBytes;
+    uint8_t* wbuf = smem + Cfg::kEpiOffset + (warp - 2) * EPI_BUFS * kEpiBufBytes;
     int uses = 0;
     const uint32_t accempty_leader = mapa_shared(smem_u32(accempty), 0);
     float alpha = 1.f;
@@ -218,7 +219,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       };
       const int row0 = tm * TM + static_cast<int>(rank) * 128 + q * 32;
       if constexpr (DIRECT_EPI) epilogue_tile_direct<OUT, TN>(tbase, p, row0 + lane, tn * TN, alpha, release);
-      else epilogue_tile<OUT, TN>(tbase, &tmC, tn * TN, row0, alpha, wbuf, uses, lane, store_pol,
+      else epilogue_tile<OUT, TN, decltype(release), EPI_BUFS>(tbase, &tmC, tn * TN, row0, alpha, wbuf, uses, lane, store_pol,
                                   (p.hints & 2) != 0, release, false, &pm, p.npeers, p.mc ? &p : nullptr);
       if (tracing) { tr_b += clock64() - w4; ++tr_c; }
     }

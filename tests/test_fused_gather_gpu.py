@@ -192,3 +192,39 @@ def test_multicast_allgather(cuda_dev, kind):
     if n < 2:
         pytest.skip("needs at least 2 GPUs")
     mp.start_processes(_mc_worker, args=(n, _free_port(), kind), nprocs=n, start_method="spawn", join=True)
+
+
+@pytest.mark.parametrize("staging", ["2", "6"])
+@pytest.mark.parametrize("kind", ["f16", "fp8"])
+def test_fused_allgather_emulated_ranks_on_one_gpu(cuda_dev, monkeypatch, staging, kind):
+    """The peer-store gather with `world` ranks emulated on one GPU: each rank's C_full is an
+    ordinary local buffer and every rank's call gets the others' buffers as its peers, so the
+    calls one after another fill every C_full. Covers both staging depths of the epilogue
+    (BW_GATHER_STAGING: 2 buffers a warp with 3 pipeline stages, or 6 with 2)."""
+    import torch
+
+    monkeypatch.setenv("BW_GATHER_STAGING", staging)
+    world, M, K, ns = 3, 520, 640, 264
+    N = ns * world
+    if kind == "f16":
+        A = torch.from_numpy(o.f16_to_f32(o.f32_to_f16(o.seeded_uniform((M, K), 331)))).to(cuda_dev).half()
+        B = torch.from_numpy(o.f16_to_f32(o.f32_to_f16(o.seeded_uniform((K, N), 332)))).to(cuda_dev).half()
+        Cs = [torch.full((M, N), float("nan"), device=cuda_dev) for _ in range(world)]
+        for r in range(world):
+            peers = [None if q == r else Cs[q].data_ptr() for q in range(world)]
+            bwgemm.gemm_f16_allgather(A, B[:, r * ns:(r + 1) * ns].contiguous(), Cs[r], peers, r)
+        want = bwgemm.gemm_f16(A, B)
+    else:
+        qa, sa = bwgemm.quantize_fp8(torch.from_numpy(o.seeded_normal((M, K), 333)).to(cuda_dev), False)
+        qb, sb = bwgemm.quantize_fp8(torch.from_numpy(o.seeded_normal((K, N), 334)).to(cuda_dev), True)
+        Cs = [torch.full((M, N), float("nan"), device=cuda_dev, dtype=torch.bfloat16) for _ in range(world)]
+        for r in range(world):
+            peers = [None if q == r else Cs[q].data_ptr() for q in range(world)]
+            bwgemm.gemm_fp8_allgather(qa, qb[r * ns:(r + 1) * ns].contiguous(), sa, sb, Cs[r], peers, r,
+                                      bwgemm.OUT_BF16)
+        want = torch.cat([bwgemm.gemm_fp8(qa, qb[r * ns:(r + 1) * ns].contiguous(), sa, sb, out_dtype=bwgemm.OUT_BF16)
+                          for r in range(world)], dim=1)
+    torch.cuda.synchronize()
+    assert bwgemm.device_status() == 0
+    for C in Cs:
+        assert torch.equal(C, want)
