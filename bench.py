@@ -400,6 +400,22 @@ def cpu_baseline(threads: int, budget_s: float = 12.0):
     return flops / dt / 1e12, f"{rows} x {N} x {K} rows of the 8192^3 fp16 GEMM, FP64 oracle, {dt:.1f} s"
 
 
+def cpu_full_1024(threads: int):
+    """The whole 1024^3 FP16 GEMM (the host-computable anchor) through the
+    FP64 oracle on host cores: TFLOP/s and seconds."""
+    import numpy as np
+
+    import oracle as o
+
+    rng = np.random.default_rng(6)
+    A = o.f16_to_f32(o.f32_to_f16(rng.uniform(-1, 1, size=(1024, 1024)).astype(np.float32)))
+    B = o.f16_to_f32(o.f32_to_f16(rng.uniform(-1, 1, size=(1024, 1024)).astype(np.float32)))
+    t0 = time.perf_counter()
+    o.gemm_f64(A, B, threads=threads)
+    dt = time.perf_counter() - t0
+    return 2.0 * 1024 ** 3 / dt / 1e12, dt
+
+
 # ---------------------------------------------------------------------------------------
 # dequantisation on the device (FP64) for the max_abs_err of the precision records
 E2M1 = [0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0, -0.0, -0.5, -1.0, -1.5, -2.0, -3.0, -4.0, -6.0]
@@ -900,8 +916,11 @@ def run_ours(args, world, rank, local):
     if rank == 0 and world == 1 and not args.no_cpu:
         threads = os.cpu_count() or 1
         v, sample = cpu_baseline(threads)
+        v1, t1 = cpu_full_1024(threads)
         line["cpu_baseline"] = {"value": round(v, 5), "unit": "TFLOP/s", "cores": threads, "kind": "port",
-                                "sample": sample, "cpu": cpu_model()}
+                                "sample": sample, "cpu": cpu_model(),
+                                "full_1024": {"tflops": round(v1, 5), "seconds": round(t1, 3),
+                                              "what": "the whole 1024^3 FP16 GEMM (configs[0]), FP64 oracle"}}
     return line
 
 

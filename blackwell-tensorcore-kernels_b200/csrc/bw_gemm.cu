@@ -240,36 +240,43 @@ bool use_narrow(int M, int N, const DeviceState& d) {
   return tiles256 < d.sms;
 }
 
-// Column-panel kernel (bw_gemm_panel.cuh) for M <= 256: the panel width W that puts every
-// 128-row x W unit on its own SM in one wave (W a multiple of 32, of 64 for an N-major B, at
-// most 512 TMEM columns), or 0 when the kernel does not apply: M > 256, K < 512, C not
-// 32-byte aligned per row (direct stores), W above 512 or below 96, or under 3/4 of the SMs
-// busy.
-// BW_PANEL = 0 disables it, 1 forces it wherever it can run.
-int panel_width(int M, int N, int K, bool gran64, const void* C, int elem, const DeviceState& d) {
+// Column-panel kernel (bw_gemm_panel.cuh) for M <= 256: the panel width W (a multiple of 32,
+// of 64 for an N-major B; MT x W <= 512 TMEM columns with MT = ceil(M / 128) accumulators) with
+// the least work per SM, ceil(panels / SMs) x W (ties go to the wider panel), among widths of at
+// least 96 x MT columns that keep 3/4 of the SMs busy; 0 when none exists or the kernel does not
+// apply: M > 256, K < 512, C not 32-byte aligned per row (direct stores). Narrow panels lose
+// because each CTA re-reads all MT x 128 rows of A (from L2) for its W columns of B: measured,
+// 128 x 8192 x 8192 FP16 at W = 64 took 47.8 us against 31.9 us split-K, W = 112..448 were 8-38%
+// faster than split-K, and 256 x 65536 x 8192 FP16 at W = 64 took 529 us against 280 us.
+// BW_PANEL = 0 disables the kernel; 1 forces it wherever it can run (any width from 32 / 64 up,
+// any number of panels); an explicit BW_SPLITK count selects split-K.
+int panel_width(int M, int N, int K, bool gran64, const void* C, int elem, const DeviceState& d, int* mt) {
   const int forced = env_int("BW_PANEL", -1);
   if (forced == 0 || M > 256 || !direct_epilogue_ok(C, N, elem)) return 0;
-  if (forced != 1 && env_int("BW_SPLITK", -1) >= 1) return 0;  // an explicit split count asks for split-K
+  if (forced != 1 && env_int("BW_SPLITK", -1) >= 1) return 0;
   if (forced != 1 && K < 512) return 0;
+  *mt = M > 128 ? 2 : 1;
   const int gran = gran64 ? 64 : 32;
-  const long tiles_m = (M + 127) / 128;
-  const long want = (static_cast<long>(N) * tiles_m + d.sms - 1) / d.sms;
-  long W = (want + gran - 1) / gran * gran;
-  if (W < gran) W = gran;
-  if (W > kPanelMaxW) return 0;
-  const long units = tiles_m * ((N + W - 1) / W);
-  if (units > d.sms) return 0;
-  // Narrow panels lose: each CTA re-reads all of A (from L2) for W columns of B, so below
-  // ~96 columns the L2 -> SM traffic of A outweighs B (measured: 128 x 8192 x 8192 FP16 at
-  // W = 64 took 47.8 us against 31.9 us split-K; W = 112..448 were 8-38% faster than split-K).
-  if (forced != 1 && (units * 4 < 3L * d.sms || W < 96)) return 0;
-  return static_cast<int>(W);
+  const int wmax = kPanelMaxW / *mt;
+  const int wmin = forced == 1 ? gran : (96 * *mt + gran - 1) / gran * gran;
+  long best_cost = -1;
+  int W = 0;
+  for (int w = wmin; w <= wmax; w += gran) {
+    const long panels = (static_cast<long>(N) + w - 1) / w;
+    if (forced != 1 && panels * 4 < 3L * d.sms) continue;
+    const long cost = (panels + d.sms - 1) / d.sms * w;
+    if (best_cost < 0 || cost <= best_cost) {
+      best_cost = cost;
+      W = w;
+    }
+  }
+  return W;
 }
 
-template <Kind KIND, bool B_MN, Out OUT>
-int launch_panel(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int W, int b_box,
-                 cudaStream_t stream) {
-  auto kern = bw_tc_gemm_panel_kernel<KIND, B_MN, OUT>;
+template <Kind KIND, bool B_MN, Out OUT, int MT>
+int launch_panel_mt(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int W, int b_box,
+                    cudaStream_t stream) {
+  auto kern = bw_tc_gemm_panel_kernel<KIND, B_MN, OUT, MT>;
   constexpr int kMaxSmem = 232448;
   static bool attr_done[64] = {};
   int dev = 0;
@@ -281,15 +288,21 @@ int launch_panel(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams&
   PanelParams pp;
   pp.W = W;
   pp.panels = (p.N + W - 1) / W;
-  pp.stage_bytes = kBM * kSlabBytes + W * kSlabBytes;
+  pp.stage_bytes = MT * kBM * kSlabBytes + W * kSlabBytes;
   pp.stages = (kMaxSmem - panel_smem_bytes(0, 0)) / pp.stage_bytes;
   if (pp.stages > kPanelMaxStages) pp.stages = kPanelMaxStages;
   if (pp.stages < 2) return set_error(BW_ERR_INVALID, "panel width %d leaves fewer than 2 stages", W);
   pp.b_box = b_box;
-  const int units = ((p.M + kBM - 1) / kBM) * pp.panels;
-  kern<<<units, kThreads, panel_smem_bytes(pp.stages, pp.stage_bytes), stream>>>(ta, tb, p, pp);
+  kern<<<pp.panels, kThreads, panel_smem_bytes(pp.stages, pp.stage_bytes), stream>>>(ta, tb, p, pp);
   BW_CUDA(cudaGetLastError());
   return BW_OK;
+}
+
+template <Kind KIND, bool B_MN, Out OUT>
+int launch_panel(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int W, int b_box, int mt,
+                 cudaStream_t stream) {
+  if (mt == 2) return launch_panel_mt<KIND, B_MN, OUT, 2>(ta, tb, p, W, b_box, stream);
+  return launch_panel_mt<KIND, B_MN, OUT, 1>(ta, tb, p, W, b_box, stream);
 }
 
 // C (BF16) = workspace (FP32; scales already applied by the split-K epilogue), 8 per thread.
@@ -393,7 +406,8 @@ int gemm_f16_impl(const void* A, const void* B, float* C, int M, int N, int K, c
   DeviceState* d;
   if ((r = ensure_device(&d)) != BW_OK) return r;
   if (K == 0) { BW_CUDA(cudaMemsetAsync(C, 0, sizeof(float) * size_t(M) * N, s)); return BW_OK; }
-  if (const int pw = g ? 0 : panel_width(M, N, K, b_mn, C, 4, *d)) {
+  int pmt = 1;
+  if (const int pw = g ? 0 : panel_width(M, N, K, b_mn, C, 4, *d, &pmt)) {
     const int box = b_mn ? 64 : (pw <= 256 ? pw : pw / 2);
     CUtensorMap ta, tb;
     if ((r = make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, A, K, M, uint64_t(K) * 2, 64, 128)) != BW_OK) return r;
@@ -402,8 +416,8 @@ int gemm_f16_impl(const void* A, const void* B, float* C, int M, int N, int K, c
     if (r != BW_OK) return r;
     GemmParams p = base_params(*d, C, M, N, K);
     p.hints = env_int("BW_L2_HINTS", 0);
-    if (b_mn) return launch_panel<Kind::F16, true, Out::F32>(ta, tb, p, pw, box, s);
-    return launch_panel<Kind::F16, false, Out::F32>(ta, tb, p, pw, box, s);
+    if (b_mn) return launch_panel<Kind::F16, true, Out::F32>(ta, tb, p, pw, box, pmt, s);
+    return launch_panel<Kind::F16, false, Out::F32>(ta, tb, p, pw, box, pmt, s);
   }
   const int splits = g ? 1 : choose_splits(M, N, (K + 63) / 64, 4, *d);
   const bool pair = g || (splits == 1 && use_pair(M, N, *d));
@@ -468,7 +482,8 @@ int gemm_fp8_impl(const uint8_t* A, const uint8_t* Bt, const float* sa, const fl
   DeviceState* d;
   if ((r = ensure_device(&d)) != BW_OK) return r;
   if (K == 0) { BW_CUDA(cudaMemsetAsync(C, 0, out_elem_bytes(out_dtype) * size_t(M) * N, s)); return BW_OK; }
-  if (const int pw = g ? 0 : panel_width(M, N, K, false, C, static_cast<int>(out_elem_bytes(out_dtype)), *d)) {
+  int pmt = 1;
+  if (const int pw = g ? 0 : panel_width(M, N, K, false, C, static_cast<int>(out_elem_bytes(out_dtype)), *d, &pmt)) {
     const int box = pw <= 256 ? pw : pw / 2;
     CUtensorMap ta, tb;
     if ((r = make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, A, K, M, uint64_t(K), 128, 128)) != BW_OK) return r;
@@ -477,8 +492,8 @@ int gemm_fp8_impl(const uint8_t* A, const uint8_t* Bt, const float* sa, const fl
     p.hints = env_int("BW_L2_HINTS", 0);
     p.scale_a = sa;
     p.scale_b = sb;
-    if (out_dtype == BW_OUT_F32) return launch_panel<Kind::F8, false, Out::F32>(ta, tb, p, pw, box, s);
-    return launch_panel<Kind::F8, false, Out::BF16>(ta, tb, p, pw, box, s);
+    if (out_dtype == BW_OUT_F32) return launch_panel<Kind::F8, false, Out::F32>(ta, tb, p, pw, box, pmt, s);
+    return launch_panel<Kind::F8, false, Out::BF16>(ta, tb, p, pw, box, pmt, s);
   }
   const int splits = g ? 1 : choose_splits(M, N, (K + 127) / 128, static_cast<int>(out_elem_bytes(out_dtype)), *d);
   const bool pair = g || (splits == 1 && use_pair(M, N, *d));

@@ -1,15 +1,18 @@
 // Column-panel tcgen05 GEMM for short-and-wide problems (M <= 256: decode-style 128 x 65536 x
 // 8192), where the cost is reading B once from HBM.
 //
-// The output is cut into tiles_m x panels units of 128 rows x W columns with W chosen on the
-// host so that every unit fits one SM and all units run in a single wave (W <= 512 = all of
-// Tensor Memory as one FP32 accumulator). Each CTA computes its unit over the whole K range:
-// no split-K, so no zeroed C, no FP32 workspace and no reduction traffic, and every B byte is
-// read exactly once. One CTA per SM (shared memory sizes it so).
-//   warp 0      TMA producer: one elected lane streams A (128 x 128 B) and the B panel
+// The output is cut into column panels of W columns; a CTA computes one panel for all MT (1 or
+// 2) 128-row blocks of M at once (MT = ceil(M / 128)), so every B slab it loads feeds MT
+// accumulators of W columns each (MT x W <= 512 = all of Tensor Memory). W is chosen on the
+// host so the panels fill the SMs in as few, as full waves as possible (one wave for M <= 128
+// and N <= 148 x 512). Each CTA runs over the whole K range: no split-K, so no zeroed C, no
+// FP32 workspace and no reduction traffic, and every B byte is read exactly once. One CTA per
+// SM (shared memory sizes it so).
+//   warp 0      TMA producer: one elected lane streams A (MT x 128 x 128 B) and the B panel
 //               (W x 128 B) per k-slab into a runtime-deep shared-memory ring.
-//   warp 1      allocates Tensor Memory; one elected lane issues, per k-step, one tcgen05.mma
-//               per 256-column chunk of the panel (N = 256 and W - 256 for W > 256).
+//   warp 1      allocates Tensor Memory; one elected lane issues, per k-step and 128-row block,
+//               one tcgen05.mma per 256-column chunk of the panel (N = 256 and W - 256 for
+//               W > 256).
 //   warps 2..5  epilogue once the last k-slab is in: tcgen05.ld 32 columns at a time, scale,
 //               convert and store 256-bit pieces of each thread's row straight to C.
 #pragma once
@@ -22,9 +25,9 @@ constexpr int kPanelMaxStages = 6;
 
 struct PanelParams {
   int W;            // panel width (columns), multiple of 32 (64 for an N-major B)
-  int panels;       // panels per 128-row block
+  int panels;       // panels (= CTAs)
   int stages;       // shared-memory ring depth
-  int stage_bytes;  // 16 KB of A + W x 128 B of B, a multiple of 1024
+  int stage_bytes;  // MT x 16 KB of A + W x 128 B of B, a multiple of 1024
   int b_box;        // rows per TMA box of a K-major B (W or W / 2)
 };
 
@@ -33,11 +36,12 @@ __host__ __device__ constexpr int panel_smem_bytes(int stages, int stage_bytes) 
   return stages * stage_bytes + (2 * kPanelMaxStages + 2) * 8 + 16 + 1024;
 }
 
-template <Kind KIND, bool B_MN, Out OUT>
+template <Kind KIND, bool B_MN, Out OUT, int MT>
 __global__ void __launch_bounds__(kThreads, 1)
     bw_tc_gemm_panel_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                             const GemmParams p, const PanelParams pp) {
   static_assert(KIND != Kind::MXF4, "panel kernel: dense kinds only");
+  static_assert(MT == 1 || MT == 2, "one or two 128-row blocks of M");
   constexpr int KE = KindTraits<KIND>::kElemsPerSlab;
   constexpr int KX = KindTraits<KIND>::kCoordPerSlab;
   extern __shared__ uint8_t smem_raw[];
@@ -53,11 +57,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int W = pp.W;
-  const int tm = blockIdx.x / pp.panels;
-  const int col0 = (blockIdx.x % pp.panels) * W;
+  const int col0 = blockIdx.x * W;
   const int nk = (p.K + KE - 1) / KE;
   const int S = pp.stages;
-  const uint32_t tmem_cols = W <= 256 ? 256u : 512u;
+  const uint32_t tmem_cols = MT * W <= 256 ? 256u : 512u;
   const WaitCtl wc{abort_flag, p.status, p.budget_ns};
 
   if (threadIdx.x == 0) {
@@ -85,9 +88,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int kb = 0; kb < nk; ++kb) {
         if (!mbar_wait(&empty[s], ph ^ 1, wc, 41)) break;
         uint8_t* sA = smem + s * pp.stage_bytes;
-        uint8_t* sB = sA + kBM * kSlabBytes;
+        uint8_t* sB = sA + MT * kBM * kSlabBytes;
         mbar_arrive_expect_tx(&full[s], tx);
-        tma_load_2d(&tmA, &full[s], sA, kb * KX, tm * kBM, pol_a);
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) tma_load_2d(&tmA, &full[s], sA + mt * kBM * kSlabBytes, kb * KX, mt * kBM, pol_a);
         if constexpr (B_MN) {
           for (int j = 0; j < W / 64; ++j)
             tma_load_2d(&tmB, &full[s], sB + j * 64 * kSlabBytes, col0 + 64 * j, kb * 64, pol_b);
@@ -111,22 +115,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(&full[s], ph, wc, 42)) { ok = false; break; }
         tc_fence_after();
         const uint32_t aaddr = smem_u32(smem + s * pp.stage_bytes);
-        const uint32_t baddr = aaddr + kBM * kSlabBytes;
+        const uint32_t baddr = aaddr + MT * kBM * kSlabBytes;
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
-          const uint64_t adesc = sdesc_sw128(aaddr + k * 32, 16, 1024);
 #pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            if (c == 1 && n1 == 0) break;
-            uint64_t bdesc;
-            // chunk c starts 256 columns in: 4 boxes of 64 columns (N-major) or 256 rows (K-major)
-            if constexpr (B_MN) bdesc = sdesc_sw128(baddr + c * 4 * 64 * kSlabBytes + k * 16 * kSlabBytes,
-                                                    64 * kSlabBytes, 1024);
-            else bdesc = sdesc_sw128(baddr + c * 256 * kSlabBytes + k * 32, 16, 1024);
-            const uint32_t d = tmem_base + c * 256;
-            if constexpr (KIND == Kind::F16) umma_f16(d, adesc, bdesc, c ? idesc1 : idesc0, acc);
-            else umma_f8f6f4(d, adesc, bdesc, c ? idesc1 : idesc0, acc);
+          for (int mt = 0; mt < MT; ++mt) {
+            const uint64_t adesc = sdesc_sw128(aaddr + mt * kBM * kSlabBytes + k * 32, 16, 1024);
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+              if (c == 1 && n1 == 0) break;
+              uint64_t bdesc;
+              // chunk c starts 256 columns in: 4 boxes of 64 columns (N-major) or 256 rows (K-major)
+              if constexpr (B_MN) bdesc = sdesc_sw128(baddr + c * 4 * 64 * kSlabBytes + k * 16 * kSlabBytes,
+                                                      64 * kSlabBytes, 1024);
+              else bdesc = sdesc_sw128(baddr + c * 256 * kSlabBytes + k * 32, 16, 1024);
+              const uint32_t d = tmem_base + mt * W + c * 256;
+              if constexpr (KIND == Kind::F16) umma_f16(d, adesc, bdesc, c ? idesc1 : idesc0, acc);
+              else umma_f8f6f4(d, adesc, bdesc, c ? idesc1 : idesc0, acc);
+            }
           }
         }
         umma_commit(&empty[s]);
@@ -144,12 +151,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (p.scale_b) alpha *= __ldg(p.scale_b);
     if (mbar_wait(accfull, 0, wc, 44)) {
       tc_fence_after();
-      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
-      const int row = tm * kBM + q * 32 + lane;
       const bool stream_out = (p.hints & 2) != 0;
       const uint64_t pol = l2_policy_evict_first();
 #pragma unroll 1
-      for (int c = 0; c < W; c += 32) {
+      for (int cc = 0; cc < MT * W; cc += 32) {
+        const int mt = cc / W, c = cc - mt * W;  // accumulator mt holds rows [128 mt, 128 mt + 128)
+        const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + mt * W;
+        const int row = mt * kBM + q * 32 + lane;
         uint32_t r[32];
         tmem_ld_32x32b_x32(tbase + c, r);
         tmem_ld_wait();

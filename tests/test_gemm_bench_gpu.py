@@ -57,3 +57,28 @@ def test_appends_reference_shaped_rows_to_a_reference_csv(tmp_path):
     assert r.returncode == 0, r.stderr
     lines = out.read_text().strip().splitlines()
     assert len(lines) == 2 and lines[1].count(",") == 9  # ten columns; the quoted device name holds no comma
+
+
+def test_reference_rows_through_bw_ref_lib(tmp_path):
+    """With BW_REF_LIB naming the reference's own launchers (built from its sources into
+    oracle/_ref), the driver adds their rows beside ours; on B200 they reproduce the
+    reference's own published max_abs_err at 1024^3 (mma_warptile/wmma 0.00376, mma_fp8 0.439),
+    and without BW_REF_LIB there are no ref_* rows at all."""
+    lib = os.path.join(REPO, "oracle", "_ref", "libref_kernels.so")
+    if not os.path.exists(lib):
+        pytest.fail(f"{lib} is missing: build it with oracle/build_ref.sh beside the reference checkout")
+    out = tmp_path / "ref.csv"
+    env = dict(os.environ, BW_INPUT_DIST="ref", BW_REF_LIB=lib)
+    names = "tc_f16,ref_wmma,ref_mma_warptile,ref_mma_fp8"
+    r = subprocess.run([BIN, "1024", "1024", "1024", str(out), names], capture_output=True, text=True, env=env,
+                       timeout=600)
+    assert r.returncode == 0, r.stdout + r.stderr
+    got = {row["kernel"]: float(row["max_abs_err"]) for row in csv.DictReader(open(out))}
+    for k, want in {"ref_wmma": 0.00376, "ref_mma_warptile": 0.00376, "ref_mma_fp8": 0.439}.items():
+        assert abs(got[k] - want) <= 1.01e-2 * want, (k, got[k], want)
+    out2 = tmp_path / "noref.csv"
+    env.pop("BW_REF_LIB")
+    r = subprocess.run([BIN, "256", "256", "256", str(out2), names], capture_output=True, text=True, env=env,
+                       timeout=300)
+    assert r.returncode == 0, r.stderr
+    assert [row["kernel"] for row in csv.DictReader(open(out2))] == ["tc_f16"]

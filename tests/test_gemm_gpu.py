@@ -507,12 +507,14 @@ def test_mxfp4_bit_identical_to_library(cuda_dev, M, N, K):
 
 
 @pytest.mark.parametrize("M,N,K", [(128, 4096, 1024), (77, 2056, 528), (200, 1024, 4096), (1, 1024, 1024),
-                                   (256, 4104, 1024), (128, 16384, 2048), (64, 9216, 512)])
+                                   (256, 4104, 1024), (128, 16384, 2048), (64, 9216, 512), (129, 8192, 1024),
+                                   (256, 40960, 512)])
 @pytest.mark.parametrize("kind", ["f16", "f16_bt", "fp8", "fp8_bf16"])
 def test_panel_kernel_parity(cuda_dev, monkeypatch, M, N, K, kind):
     """The column-panel kernel for short-and-wide problems (forced with BW_PANEL=1): panel
-    widths from 32 to 512 columns (two MMAs per k-step above 256), ragged M / N / K, both B
-    layouts of FP16, FP32 and BF16 C."""
+    widths from 32 to 512 columns (two MMAs per k-step above 256), one or two 128-row blocks of
+    M per panel (M > 128), more panels than SMs (two waves), ragged M / N / K, both B layouts of
+    FP16, FP32 and BF16 C."""
     import torch
 
     monkeypatch.setenv("BW_PANEL", "1")
