@@ -3,6 +3,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload f16|fp8|mxfp4|fp4] [--shape MxNxK] [--no-extra] [--no-compare]
+                    [--no-cpu] [--multicast]
 
 A step is one GEMM over one batch of synthetic inputs already resident in HBM:
   N = 1: C = A x B at M = N = K = 8192 (FP16 in, FP32 accumulate,
@@ -25,8 +26,9 @@ Sub-records of the same line:
              row timed interleaved, max_abs_err against an FP64 GEMM of the dequantised inputs.
   sharded    (every N) BASELINE configs[4]: 16384 x 65536 x 8192 split column-wise over the N
              ranks (strong scaling), FP16 -> FP32 and FP8 -> BF16: GEMM alone, and for N > 1
-             GEMM + fused all-gather (one kernel) and GEMM + NCCL all-gather + unshard; plus
-             the skinny 128 x 65536 x 8192 on the same sharding.
+             GEMM + fused all-gather (one kernel) and GEMM + NCCL all-gather + unshard (with
+             --multicast also the fused gather through NVSwitch multicast); plus the skinny
+             128 x 65536 x 8192 on the same sharding.
 
 --impl reference runs the reference's own stock launcher (launch_mma_warptile, its headline
 FP16 kernel, built from its sources for sm_100a by oracle/build_ref.sh) through its launch_*
